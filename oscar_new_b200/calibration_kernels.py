@@ -1,0 +1,98 @@
+"""OSCAR calibration operators on B200 (reference ``oscar_ascend/calibration_kernels.py``).
+
+Same names and meaning as the reference: ``accumulate_gram``, ``sst_weights``,
+``normalize``, ``calibrated_rotations``.  The eigensolver runs every Jacobi sweep in a
+single launch (one 8-CTA thread-block cluster per matrix) and returns its convergence
+info; only that small info vector is read back to decide success, as the reference
+reads one residual scalar.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("calibration kernels run on a CUDA device only")
+
+
+def accumulate_gram(x: torch.Tensor, covariance: torch.Tensor, weights: torch.Tensor | None = None):
+    """``covariance += X^T X`` over all rows/heads of bf16 ``x`` [n, h, 256], or the
+    ``weights``-weighted sum (reference calibration_kernels.py:59-70)."""
+    _cuda(x, covariance, weights)
+    if covariance.dtype != torch.float32 or covariance.shape != (256, 256) or not covariance.is_contiguous():
+        raise ValueError("covariance must be contiguous fp32 [256, 256]")
+    n, h, d = x.shape
+    if d != 256:
+        raise ValueError("head_dim must be 256")
+    if x.dtype != torch.bfloat16 or x.stride(2) != 1 or x.stride(0) % 8 or x.stride(1) % 8 or x.data_ptr() % 16:
+        x = x.to(torch.bfloat16).contiguous()
+    w = None
+    if weights is not None:
+        w = weights.float().contiguous().view(-1)
+        if w.numel() != n * h:
+            raise ValueError("weights must have one entry per (token, head) row")
+    _lib.call("oscar_accumulate_gram", x.data_ptr(), n, h, x.stride(0), x.stride(1),
+              None if w is None else w.data_ptr(), covariance.data_ptr(), _stream(x))
+
+
+def sst_weights(key: torch.Tensor, q_covariance: torch.Tensor, total_weight: torch.Tensor):
+    """``w_t = max(k_t C k_t^T, 0)`` per row and ``total_weight += sum w``
+    (reference calibration_kernels.py:109-126; any number of KV heads)."""
+    _cuda(key, q_covariance, total_weight)
+    n, h, d = key.shape
+    if key.dtype != torch.bfloat16:
+        key = key.to(torch.bfloat16)
+    c = q_covariance.float().contiguous()
+    weights = torch.empty(n * h, device=key.device, dtype=torch.float32)
+    _lib.call("oscar_sst_weights", key.data_ptr(), n, h, key.stride(0), key.stride(1), c.data_ptr(),
+              weights.data_ptr(), total_weight.data_ptr(), _stream(key))
+    return weights
+
+
+def normalize(x: torch.Tensor, denominator):
+    """``x / max(denominator, 1e-30)`` with a host or device denominator (reference :145-156)."""
+    _cuda(x)
+    out = torch.empty_like(x)
+    xc = x.contiguous()
+    dev = isinstance(denominator, torch.Tensor)
+    _lib.call("oscar_normalize", xc.data_ptr(), xc.numel(), denominator.data_ptr() if dev else None,
+              0.0 if dev else float(denominator), out.data_ptr(), _stream(xc))
+    return out
+
+
+def calibrated_rotations(covariances: torch.Tensor, max_sweeps: int = 12, tolerance: float = 1e-6):
+    """Batched cyclic Jacobi + ``U H P_br`` (reference :287-327).
+
+    Returns ``(rotations [B,256,256], eigenvalues [B,256], info)``; raises like the
+    reference when the result is non-finite or did not converge.
+    """
+    _cuda(covariances)
+    if covariances.dtype != torch.float32:
+        raise ValueError("calibration eigensolver requires fp32 covariances")
+    batch, dim, last = covariances.shape
+    if dim != 256 or last != 256:
+        raise ValueError("calibration eigensolver is scoped to D256")
+    cov = covariances.contiguous()
+    rot = torch.empty_like(cov)
+    evals = torch.empty((batch, dim), dtype=torch.float32, device=cov.device)
+    info = torch.zeros((batch, 4), dtype=torch.float32, device=cov.device)
+    _lib.call("oscar_jacobi_rotations", cov.data_ptr(), batch, int(max_sweeps), float(tolerance), rot.data_ptr(),
+              evals.data_ptr(), info.data_ptr(), _stream(cov))
+    host = info.cpu()
+    status = host[:, 2]
+    residual = float(host[:, 1].max())
+    result = {"sweeps": int(host[:, 0].max()), "relative_off_diagonal": residual}
+    if bool((status == 2).any()):
+        raise RuntimeError("non-finite calibration covariance; rotations not published")
+    if bool((status != 0).any()):
+        raise RuntimeError(f"calibration eigensolver did not converge: {residual}; rotations not published")
+    return rot, evals, result

@@ -1,0 +1,1201 @@
+// Paged split-KV decode attention over the OSCAR cache (reference
+// oscar_ascend/kernels.py:290-482), split LSE merge (:485-511), path merge (:514-541),
+// BF16 window store (:544-620) and the compact task table (:222-287).
+//
+// History kernel (INT2, rotated space).  One CTA = one (task, split, head group).
+// A producer warp streams 128-token kernel blocks of the paged K stripe into a
+// 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk, mbarrier
+// completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast).
+// Consumer warps own (KV head, 8 query rows) units and 16-token m-tiles.
+//
+// Dequantisation is factored out of the MMA: k = c*s + z per token, so
+//   q.k   = s * (q.c) + z * sum(q)          and   sum_t p_t v_t = sum_t (p_t s_t) c_t + sum_t p_t z_t.
+// Only the 2-bit codes enter the tensor cores, as fp16 subnormals: a single AND of
+// a packed 32-bit code word with 0x00030003 << 2p leaves two codes at bit 2p of each
+// half, i.e. the fp16 values c * 4^p * 2^-24, exactly.  The query is pre-divided by
+// 4^p (and the output multiplied back), so one LOP3 turns 4 codes of a word into
+// MMA operand halves with no conversion arithmetic.  The contraction dimension is
+// permuted (a bijection over the 256 dims) so that each lane reads only its own 16
+// bytes of a token vector; the query fragment uses the same permutation.
+// MMAs use the swapped orientation (tokens / dims as M = 16, query rows as N = 8).
+#include <algorithm>
+
+#include "common.cuh"
+#include "rowgemm.cuh"
+
+namespace oscar {
+
+constexpr int kStages = 4;
+constexpr int kMaxConsumerWarps = 16;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kTwo24 = 16777216.0f;
+constexpr float kRescaleSlack = 3.0f;  // lazily re-base the running max (p <= 2^3)
+
+struct HistParams {
+  const __nv_bfloat16 *query;  // rotated query rows, unit inner stride
+  int64_t qs0, qs1;
+  const uint8_t *history;
+  const int32_t *qstarts, *seq_lens, *table, *counts, *tasks, *task_count;
+  int32_t num_tasks;
+  float *partials;  // [n, Hq, split_slots, 256]
+  float *lse;       // [n, Hq, split_slots]
+  int32_t split_slots;
+  int32_t splits;
+  oscar_geometry geo;
+  float scale_log2;
+  // launch shape
+  int32_t heads_per_cta;  // HPC
+  int32_t ntiles;         // 8-row n-tiles per head
+  int32_t units;          // HPC * ntiles
+  int32_t warps_per_unit; // R_tok
+  int32_t consumers;      // units * warps_per_unit
+  int32_t chunk_tokens;   // CT
+  int32_t stage_bytes;
+  int32_t *status;        // nullable error word
+};
+
+struct TaskInfo {
+  bool live;
+  int req, qoff, qstart, qlen, prefix, sink_len, recent_begin;
+};
+
+OSCAR_DEVINL TaskInfo load_task(int task, const int32_t *tasks, const int32_t *task_count,
+                                const int32_t *qstarts, const int32_t *seq_lens, const int32_t *counts,
+                                const oscar_geometry &g) {
+  TaskInfo ti{};
+  ti.live = task < task_count[0];
+  if (!ti.live) return ti;
+  ti.req = tasks[2 * task];
+  ti.qoff = tasks[2 * task + 1];
+  ti.qstart = qstarts[ti.req];
+  const int qend = min(qstarts[ti.req + 1], counts[1]);
+  ti.qlen = qend - ti.qstart;
+  const int seq = seq_lens[ti.req];
+  ti.prefix = seq - ti.qlen;
+  ti.sink_len = min(g.sink, ti.prefix);
+  ti.recent_begin = max(ti.sink_len, ti.prefix - g.recent);
+  return ti;
+}
+
+// Query operands of one 8-row n-tile, in the permuted contraction order the key codes
+// are read in (lane t owns dims [64t, 64t+64)):
+//  * qf[js]: fp16 fragments of the exact code functional sum_d q_d c_d, k-step js = 4i+p
+//    covering dims 16(4t+i) + {p, 8+p | 4+p, 12+p}, pre-divided by 4^p;
+//  * qb[j]:  int8 fragments (per-row scale) of the bit functionals, k32-step j = 2i+h
+//    covering dims 16(4t+i) + 4b + 2h (+1 for the second register), b = 0..3;
+//  * qsum / qscale of the rows 2t, 2t+1 this lane accumulates.
+struct QueryFrags {
+  uint32_t qf[16][2];
+  uint32_t qb[8][2];
+  float qsum[2];
+  float qscale[2];
+};
+
+OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, bool valid) {
+  const int lane = threadIdx.x & 31, t = lane & 3;
+  uint32_t w[32];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 v = valid ? *reinterpret_cast<const uint4 *>(qrow + 64 * t + 8 * c) : make_uint4(0, 0, 0, 0);
+    w[4 * c] = v.x, w[4 * c + 1] = v.y, w[4 * c + 2] = v.z, w[4 * c + 3] = v.w;
+  }
+  auto dim = [&](int d) {  // bf16 value of local dim d (0..63)
+    const uint32_t word = w[d >> 1];
+    return bf16_bits_to_float((d & 1) ? (word >> 16) : (word & 0xffffu));
+  };
+  float s = 0.f, amax = 0.f;
+#pragma unroll
+  for (int d = 0; d < 64; ++d) {
+    s += dim(d);
+    amax = fmaxf(amax, fabsf(dim(d)));
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float mul = 1.0f / (float)(1 << (2 * p));
+      Q.qf[4 * i + p][0] = pack_half2(dim(16 * i + p) * mul, dim(16 * i + 8 + p) * mul);
+      Q.qf[4 * i + p][1] = pack_half2(dim(16 * i + 4 + p) * mul, dim(16 * i + 12 + p) * mul);
+    }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const float scale = amax / 127.0f;
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  auto q8 = [&](int d) { return (uint32_t)(min(max(__float2int_rn(dim(d) * inv), -127), 127) & 0xff); };
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t r0 = 0, r1 = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        r0 |= q8(16 * i + 4 * b + 2 * h) << (8 * b);
+        r1 |= q8(16 * i + 4 * b + 2 * h + 1) << (8 * b);
+      }
+      Q.qb[2 * i + h][0] = r0;
+      Q.qb[2 * i + h][1] = r1;
+    }
+  // s / scale are row-gi values on all four t lanes; the S fragment needs rows 2t, 2t+1.
+  Q.qsum[0] = __shfl_sync(0xffffffffu, s, 8 * t);
+  Q.qsum[1] = __shfl_sync(0xffffffffu, s, 8 * t + 4);
+  Q.qscale[0] = __shfl_sync(0xffffffffu, scale, 8 * t);
+  Q.qscale[1] = __shfl_sync(0xffffffffu, scale, 8 * t + 4);
+}
+
+// Per-token coefficients of q.k with k = bf16(c*s + z) (the reference rounds the
+// dequantised key to bf16):  q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
+// with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.
+struct KeyCoef {
+  float v0, d1, a, b;
+};
+
+OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
+  const float s = half_bits_to_float(sz & 0xffffu), z = half_bits_to_float(sz >> 16);
+  const float v0 = round_bf16(z);
+  const float v1 = round_bf16(__fadd_rn(s, z));
+  const float v2 = round_bf16(__fadd_rn(2.f * s, z));
+  const float v3 = round_bf16(__fadd_rn(3.f * s, z));
+  KeyCoef k;
+  k.v0 = v0;
+  k.d1 = v1 - v0;
+  k.a = (v2 - v1) - (v1 - v0);
+  k.b = (v3 - v2) - (v1 - v0);
+  return k;
+}
+
+template <int MAXW>
+__global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(HistParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const oscar_geometry &g = P.geo;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int task = blockIdx.x, split = blockIdx.y;
+  const int h0 = blockIdx.z * P.heads_per_cta;
+  const TaskInfo ti = load_task(task, P.tasks, P.task_count, P.qstarts, P.seq_lens, P.counts, g);
+  if (!ti.live || ti.qlen <= 0) return;
+  const int rows_valid = min(g.query_tile, ti.qlen - ti.qoff) * g.group;
+  const int length = ti.recent_begin - ti.sink_len;
+  const int tiles = (length + 31) / 32;
+  const int per_split = (tiles + P.splits - 1) / P.splits;
+  const int begin = split * per_split * 32;
+  const int end = min((split + 1) * per_split * 32, length);
+  const int lo = ti.sink_len + begin, hi = ti.sink_len + max(end, begin);  // absolute positions
+  const int CT = P.chunk_tokens;
+  const int first_chunk = lo / CT;
+  const int nchunks = hi > lo ? (hi - 1) / CT - first_chunk + 1 : 0;
+
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + kStages;
+  uint8_t *stages = smem + 128;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], P.consumers);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  const int hpc = P.heads_per_cta;
+  const int token_bytes = hpc * g.slot_bytes;
+  if (warp == P.consumers) {
+    // ---------------- producer warp ----------------
+    if (lane == 0) {
+      const int32_t *trow = P.table + (int64_t)ti.req * g.table_stride;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kStages;
+        if (c >= kStages && !mbar_wait_bounded(&empty[s], ((c / kStages) - 1) & 1)) {
+          if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
+          break;
+        }
+        const int pos = (first_chunk + c) * CT;
+        const int64_t slot0 = (int64_t)trow[pos / kKernelBlock] * kKernelBlock + pos % kKernelBlock;
+        const uint8_t *src = P.history + (slot0 / g.block_tokens) * g.page_bytes +
+                             ((slot0 % g.block_tokens) * g.kv_heads + h0) * (int64_t)g.slot_bytes;
+        const uint32_t dst = smem_u32(stages + s * P.stage_bytes);
+        mbar_arrive_expect_tx(&full[s], CT * token_bytes);
+        if (hpc == g.kv_heads) {
+          bulk_copy_g2s(dst, src, CT * token_bytes, &full[s]);
+        } else {
+          for (int tk = 0; tk < CT; ++tk)
+            bulk_copy_g2s(dst + tk * token_bytes, src + (int64_t)tk * g.kv_heads * g.slot_bytes, token_bytes,
+                          &full[s]);
+        }
+      }
+    }
+    return;
+  }
+  if (warp > P.consumers) return;
+
+  // ---------------- consumer warps ----------------
+  const int unit = warp % P.units, sub = warp / P.units;
+  const int head_local = unit / P.ntiles, ntile = unit % P.ntiles;
+  const int head = h0 + head_local;
+  const int gi = lane >> 2, t = lane & 3;
+  // query row of this thread's B fragment: row index r = 8*ntile + gi
+  const int r_mine = 8 * ntile + gi;
+  const bool rvalid = r_mine < rows_valid;
+  const int qtok = ti.qstart + ti.qoff + r_mine / g.group;
+  const int qhead = head * g.group + r_mine % g.group;
+  QueryFrags Q;
+  load_query_frags(Q, P.query + (int64_t)qtok * P.qs0 + (int64_t)qhead * P.qs1, rvalid);
+
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f}, zp_run[2] = {0.f, 0.f};
+  const float sl2 = P.scale_log2;
+  const int mtiles = CT / 16;
+  bool ok = true;
+
+#pragma unroll 1
+  for (int c = 0; c < nchunks && ok; ++c) {
+    const int s = c % kStages;
+    if (!mbar_wait_bounded(&full[s], (c / kStages) & 1)) {
+      ok = false;
+      if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
+      break;
+    }
+    const uint8_t *stage = stages + s * P.stage_bytes;
+    const int cpos = (first_chunk + c) * CT;
+#pragma unroll 1
+    for (int mt = sub; mt < mtiles; mt += P.warps_per_unit) {
+      const int tpos = cpos + 16 * mt;
+      if (tpos + 16 <= lo || tpos >= hi) continue;  // warp-uniform
+      const uint8_t *tile = stage + (16 * mt) * token_bytes + head_local * g.slot_bytes;
+      // ---- S^T (tokens x rows): exact sum q c on fp16, bit functionals on int8 ----
+      const uint4 ka = *reinterpret_cast<const uint4 *>(tile + gi * token_bytes + 16 * t);
+      const uint4 kb = *reinterpret_cast<const uint4 *>(tile + (gi + 8) * token_bytes + 16 * t);
+      const uint32_t kaw[4] = {ka.x, ka.y, ka.z, ka.w}, kbw[4] = {kb.x, kb.y, kb.z, kb.w};
+      float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
+      int cb[4] = {0, 0, 0, 0}, cc[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t a_sh = kaw[i] >> 8, b_sh = kbw[i] >> 8;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t msk = 0x00030003u << (2 * p);
+          mma_f16_16816((p & 1) ? sd : sc, kaw[i] & msk, kbw[i] & msk, a_sh & msk, b_sh & msk, Q.qf[4 * i + p][0],
+                        Q.qf[4 * i + p][1]);
+        }
+        const uint32_t a1 = kaw[i] >> 1, b1 = kbw[i] >> 1;  // bit 0 of each pair -> high bits b1
+        const uint32_t ay = kaw[i] & a1, by = kbw[i] & b1;  // b0 & b1 at the even bits
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int p0 = 2 * h, p1 = 2 * h + 1;
+          mma_s8_16832(cb, (a1 >> (2 * p0)) & 0x01010101u, (b1 >> (2 * p0)) & 0x01010101u,
+                       (a1 >> (2 * p1)) & 0x01010101u, (b1 >> (2 * p1)) & 0x01010101u, Q.qb[2 * i + h][0],
+                       Q.qb[2 * i + h][1]);
+          mma_s8_16832(cc, (ay >> (2 * p0)) & 0x01010101u, (by >> (2 * p0)) & 0x01010101u,
+                       (ay >> (2 * p1)) & 0x01010101u, (by >> (2 * p1)) & 0x01010101u, Q.qb[2 * i + h][0],
+                       Q.qb[2 * i + h][1]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] += sd[e];
+      // ---- logits (log2 domain) ----
+      const uint32_t kszA = *reinterpret_cast<const uint32_t *>(tile + gi * token_bytes + 64);
+      const uint32_t kszB = *reinterpret_cast<const uint32_t *>(tile + (gi + 8) * token_bytes + 64);
+      const uint32_t vszA = *reinterpret_cast<const uint32_t *>(tile + gi * token_bytes + g.vector_bytes + 64);
+      const uint32_t vszB = *reinterpret_cast<const uint32_t *>(tile + (gi + 8) * token_bytes + g.vector_bytes + 64);
+      const bool va = tpos + gi >= lo && tpos + gi < hi;
+      const bool vb = tpos + gi + 8 >= lo && tpos + gi + 8 < hi;
+      const KeyCoef ca = key_coefficients(kszA), cbk = key_coefficients(kszB);
+      float lg[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const KeyCoef &kc = e < 2 ? ca : cbk;
+        const int r = e & 1;
+        float dot = kc.v0 * Q.qsum[r];
+        dot = fmaf(kc.d1 * kTwo24, sc[e], dot);
+        dot = fmaf(kc.a * Q.qscale[r], (float)cb[e], dot);
+        dot = fmaf(kc.b * Q.qscale[r], (float)cc[e], dot);
+        lg[e] = ((e < 2) ? va : vb) ? dot * sl2 : -INFINITY;
+      }
+      // ---- online softmax with lazy re-basing ----
+      float mx[2] = {fmaxf(lg[0], lg[2]), fmaxf(lg[1], lg[3])};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 4));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 8));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 16));
+      }
+      const bool need0 = mx[0] > m_run[0] + kRescaleSlack || (m_run[0] == -INFINITY && mx[0] > -INFINITY);
+      const bool need1 = mx[1] > m_run[1] + kRescaleSlack || (m_run[1] == -INFINITY && mx[1] > -INFINITY);
+      if (__any_sync(0xffffffffu, need0 || need1)) {
+        const float a0 = need0 ? (m_run[0] == -INFINITY ? 0.f : ex2(m_run[0] - mx[0])) : 1.f;
+        const float a1 = need1 ? (m_run[1] == -INFINITY ? 0.f : ex2(m_run[1] - mx[1])) : 1.f;
+        if (need0) m_run[0] = mx[0];
+        if (need1) m_run[1] = mx[1];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          o[i][0] *= a0, o[i][1] *= a1, o[i][2] *= a0, o[i][3] *= a1;
+        }
+        l_run[0] *= a0, l_run[1] *= a1, zp_run[0] *= a0, zp_run[1] *= a1;
+      }
+      const float ms0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
+      const float ms1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
+      const float p0 = ex2(lg[0] - ms0), p1 = ex2(lg[1] - ms1), p2 = ex2(lg[2] - ms0), p3 = ex2(lg[3] - ms1);
+      const float vsA = va ? half_bits_to_float(vszA & 0xffffu) : 0.f;
+      const float vzA = va ? half_bits_to_float(vszA >> 16) : 0.f;
+      const float vsB = vb ? half_bits_to_float(vszB & 0xffffu) : 0.f;
+      const float vzB = vb ? half_bits_to_float(vszB >> 16) : 0.f;
+      l_run[0] += p0 + p2;
+      l_run[1] += p1 + p3;
+      zp_run[0] = fmaf(p0, vzA, fmaf(p2, vzB, zp_run[0]));
+      zp_run[1] = fmaf(p1, vzA, fmaf(p3, vzB, zp_run[1]));
+      // P'^T fragments: (token, row) -> transposed to (row, token)
+      const uint32_t pb0 = movmatrix_trans(pack_half2(p0 * vsA, p1 * vsA));
+      const uint32_t pb1 = movmatrix_trans(pack_half2(p2 * vsB, p3 * vsB));
+      // ---- O^T += Vc^T . P'^T (dims x rows) ----
+      const uint8_t *vt = tile + g.vector_bytes;
+      uint32_t vw[4][2];  // [token 2t,2t+1,2t+8,2t+9][word 2gi, 2gi+1]
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int tok = 2 * t + (q & 1) + (q >> 1) * 8;
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(vt + tok * token_bytes) + 2 * gi;
+        vw[q][0] = src[0];
+        vw[q][1] = src[1];
+      }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t sel = (uint32_t)b | ((uint32_t)(4 + b) << 8);
+        const uint32_t x0 = prmt(vw[0][0], vw[1][0], sel);  // word 2gi, tokens 2t,2t+1
+        const uint32_t x1 = prmt(vw[0][1], vw[1][1], sel);  // word 2gi+1
+        const uint32_t x2 = prmt(vw[2][0], vw[3][0], sel);  // word 2gi, tokens 2t+8,2t+9
+        const uint32_t x3 = prmt(vw[2][1], vw[3][1], sel);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t msk = 0x00030003u << (2 * p);
+          mma_f16_16816(o[4 * b + p], x0 & msk, x1 & msk, x2 & msk, x3 & msk, pb0, pb1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---------------- combine the warps of a unit, write the partial ----------------
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 4);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 8);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 16);
+    zp_run[r] += __shfl_xor_sync(0xffffffffu, zp_run[r], 4);
+    zp_run[r] += __shfl_xor_sync(0xffffffffu, zp_run[r], 8);
+    zp_run[r] += __shfl_xor_sync(0xffffffffu, zp_run[r], 16);
+  }
+  // every consumer warp is past its last stage read; reuse the stage ring
+  asm volatile("bar.sync 1, %0;" ::"r"(P.consumers * 32));
+  // exchange area over the stage ring: one record (O^T fragment + running max) per
+  // non-leader warp, then l / zp of every consumer warp
+  float *xch = reinterpret_cast<float *>(stages);
+  constexpr int kSlot = 16 * 4 * 32 + 2 * 32;  // floats per warp record
+  if (sub > 0) {
+    float *rec = xch + (size_t)(warp - P.units) * kSlot;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rec[(i * 4 + q) * 32 + lane] = o[i][q];
+    rec[2048 + lane] = m_run[0];
+    rec[2048 + 32 + lane] = m_run[1];
+  }
+  float *aux = xch + (size_t)(P.consumers - P.units) * kSlot;  // [warp][4][32]
+  aux[(warp * 4 + 0) * 32 + lane] = l_run[0];
+  aux[(warp * 4 + 1) * 32 + lane] = l_run[1];
+  aux[(warp * 4 + 2) * 32 + lane] = zp_run[0];
+  aux[(warp * 4 + 3) * 32 + lane] = zp_run[1];
+  asm volatile("bar.sync 1, %0;" ::"r"(P.consumers * 32));
+  if (sub > 0) return;
+  float mtot[2] = {m_run[0], m_run[1]};
+  for (int w2 = warp + P.units; w2 < P.consumers; w2 += P.units) {
+    const float *rec = xch + (size_t)(w2 - P.units) * kSlot;
+    mtot[0] = fmaxf(mtot[0], rec[2048 + lane]);
+    mtot[1] = fmaxf(mtot[1], rec[2048 + 32 + lane]);
+  }
+  float f0 = m_run[0] == -INFINITY ? 0.f : ex2(m_run[0] - mtot[0]);
+  float f1 = m_run[1] == -INFINITY ? 0.f : ex2(m_run[1] - mtot[1]);
+  float L[2] = {l_run[0] * f0, l_run[1] * f1}, Z[2] = {zp_run[0] * f0, zp_run[1] * f1};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] *= f0, o[i][1] *= f1, o[i][2] *= f0, o[i][3] *= f1;
+  for (int w2 = warp + P.units; w2 < P.consumers; w2 += P.units) {
+    const float *rec = xch + (size_t)(w2 - P.units) * kSlot;
+    const float mw0 = rec[2048 + lane], mw1 = rec[2048 + 32 + lane];
+    const float e0 = mw0 == -INFINITY ? 0.f : ex2(mw0 - mtot[0]);
+    const float e1 = mw1 == -INFINITY ? 0.f : ex2(mw1 - mtot[1]);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[i][0] = fmaf(e0, rec[(i * 4 + 0) * 32 + lane], o[i][0]);
+      o[i][1] = fmaf(e1, rec[(i * 4 + 1) * 32 + lane], o[i][1]);
+      o[i][2] = fmaf(e0, rec[(i * 4 + 2) * 32 + lane], o[i][2]);
+      o[i][3] = fmaf(e1, rec[(i * 4 + 3) * 32 + lane], o[i][3]);
+    }
+    L[0] = fmaf(e0, aux[(w2 * 4 + 0) * 32 + lane], L[0]);
+    L[1] = fmaf(e1, aux[(w2 * 4 + 1) * 32 + lane], L[1]);
+    Z[0] = fmaf(e0, aux[(w2 * 4 + 2) * 32 + lane], Z[0]);
+    Z[1] = fmaf(e1, aux[(w2 * 4 + 3) * 32 + lane], Z[1]);
+  }
+  // rows of this thread: 8*ntile + 2t + {0,1}; dims 32gi + {0..15} and 32gi + 16 + {0..15}
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = 8 * ntile + 2 * t + r;
+    if (row >= rows_valid) continue;
+    const int tok = ti.qstart + ti.qoff + row / g.group;
+    const int qh = head * g.group + row % g.group;
+    const int64_t orow = ((int64_t)tok * g.kv_heads * g.group + qh) * P.split_slots + split;
+    const bool any = L[r] > 0.f;
+    const float inv = any ? 1.0f / L[r] : 0.f;
+    const float zterm = any ? Z[r] * inv : 0.f;
+    float *dst = P.partials + orow * kDim + 32 * gi;
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int mv = 4 * q4 + e;  // dim offset delta = mv, position p = e
+          const float mul = kTwo24 / (float)(1 << (2 * e));
+          v[e] = fmaf(o[mv][2 * half + r] * mul, inv, zterm);
+        }
+        *reinterpret_cast<float4 *>(dst + 16 * half + 4 * q4) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    // lse (natural log): m is in log2 units
+    if (gi == 0) P.lse[orow] = any ? (mtot[r] * 0.69314718055994531f + logf(L[r])) : -INFINITY;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// BF16 raw path: sink + recent (window) + causal current tokens, one split.
+// One CTA = (task, KV head, 8-row n-tile); 4 warps split the token list.
+// ----------------------------------------------------------------------------
+struct RawParams {
+  const __nv_bfloat16 *query;
+  int64_t qs0, qs1;
+  const __nv_bfloat16 *key, *value;
+  int64_t ks0, ks1, vs0, vs1;
+  const __nv_bfloat16 *window;
+  const int32_t *qstarts, *seq_lens, *table, *counts, *tasks, *task_count;
+  float *partials, *lse;
+  int32_t split_slots, split_index;
+  oscar_geometry geo;
+  float scale_log2;
+  int32_t ntiles;
+};
+
+constexpr int kRawWarps = 4;
+constexpr int kRawSmem = kRawWarps * 2 * 16 * kDim * 2;  // per warp K and V 16-token tiles
+
+OSCAR_DEVINL const __nv_bfloat16 *raw_token_row(const RawParams &P, const TaskInfo &ti, int64_t owner,
+                                                int idx, int kv, int head) {
+  // idx-th token of the raw list: sink | prefix recent | current
+  const oscar_geometry &g = P.geo;
+  const int nprev = ti.sink_len + ti.prefix - ti.recent_begin;
+  if (idx < nprev) {
+    const int pos = idx < ti.sink_len ? idx : ti.recent_begin + idx - ti.sink_len;
+    return P.window + window_elem_offset(owner, window_index(pos, g), kv, head, g);
+  }
+  const int cur = ti.qstart + idx - nprev;
+  return kv == 0 ? P.key + (int64_t)cur * P.ks0 + (int64_t)head * P.ks1
+                 : P.value + (int64_t)cur * P.vs0 + (int64_t)head * P.vs1;
+}
+
+__global__ void __launch_bounds__(32 * kRawWarps) raw_attention_kernel(RawParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const oscar_geometry &g = P.geo;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gi = lane >> 2, t = lane & 3;
+  const int task = blockIdx.x, head = blockIdx.y, ntile = blockIdx.z;
+  const TaskInfo ti = load_task(task, P.tasks, P.task_count, P.qstarts, P.seq_lens, P.counts, g);
+  if (!ti.live || ti.qlen <= 0) return;
+  const int rows_valid = min(g.query_tile, ti.qlen - ti.qoff) * g.group;
+  if (8 * ntile >= rows_valid) return;
+  const int nprev = ti.sink_len + ti.prefix - ti.recent_begin;
+  const int total = nprev + ti.qlen;
+  const int64_t owner = (int64_t)P.table[(int64_t)ti.req * g.table_stride] / (g.block_tokens / kKernelBlock);
+  // query fragment (unrotated bf16), row r = 8*ntile + gi
+  const int r_mine = 8 * ntile + gi;
+  const bool rvalid = r_mine < rows_valid;
+  const int qi_mine = ti.qoff + r_mine / g.group;
+  const __nv_bfloat16 *qrow = P.query + (int64_t)(ti.qstart + qi_mine) * P.qs0 +
+                              (int64_t)(head * g.group + r_mine % g.group) * P.qs1;
+  uint32_t qf[16][2];
+#pragma unroll
+  for (int js = 0; js < 16; ++js) {
+    qf[js][0] = rvalid ? *reinterpret_cast<const uint32_t *>(qrow + 16 * js + 2 * t) : 0u;
+    qf[js][1] = rvalid ? *reinterpret_cast<const uint32_t *>(qrow + 16 * js + 8 + 2 * t) : 0u;
+  }
+  // causal limit for rows 2t, 2t+1 (query index of the row)
+  int qlim[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = 8 * ntile + 2 * t + r;
+    qlim[r] = ti.prefix + ti.qoff + row / g.group;
+  }
+  __nv_bfloat16 *sk = reinterpret_cast<__nv_bfloat16 *>(smem) + warp * 2 * 16 * kDim;
+  __nv_bfloat16 *sv = sk + 16 * kDim;
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+#pragma unroll 1
+  for (int base = 16 * warp; base < total; base += 16 * kRawWarps) {
+    // stage 16 K and V rows (swizzled 16-byte chunks)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int c = lane + 32 * i;  // 16 rows x 32 chunks
+      const int r = c >> 5, ch = c & 31;
+      const int idx = base + r;
+      __nv_bfloat16 *dk = sk + r * kDim + ((ch ^ (r & 7)) << 3);
+      __nv_bfloat16 *dv = sv + r * kDim + ((ch ^ (r & 7)) << 3);
+      if (idx < total) {
+        cp_async_16(smem_u32(dk), raw_token_row(P, ti, owner, idx, 0, head) + ch * 8);
+        cp_async_16(smem_u32(dv), raw_token_row(P, ti, owner, idx, 1, head) + ch * 8);
+      } else {
+        *reinterpret_cast<uint4 *>(dk) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(dv) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int js = 0; js < 16; ++js) {
+      uint32_t a[4];
+      const int row = lane & 15, k = 16 * js + (lane >> 4) * 8;
+      ldmatrix_x4(a, smem_u32(sk + row * kDim + (((k >> 3) ^ (row & 7)) << 3)));
+      mma_bf16_16816(sc, a[0], a[1], a[2], a[3], qf[js][0], qf[js][1]);
+    }
+    // positions of tokens gi, gi+8
+    float lg[4];
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb) {
+      const int idx = base + gi + 8 * hb;
+      int pos;
+      if (idx < ti.sink_len) pos = idx;
+      else if (idx < nprev) pos = ti.recent_begin + idx - ti.sink_len;
+      else pos = ti.prefix + idx - nprev;
+      const bool ok = idx < total;
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+        lg[2 * hb + r] = (ok && pos <= qlim[r]) ? sc[2 * hb + r] * P.scale_log2 : -INFINITY;
+    }
+    float mx[2] = {fmaxf(lg[0], lg[2]), fmaxf(lg[1], lg[3])};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 4));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 8));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 16));
+    }
+    float a[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float mn = fmaxf(m_run[r], mx[r]);
+      a[r] = (m_run[r] == -INFINITY) ? 0.f : ex2(m_run[r] - mn);
+      m_run[r] = mn;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] *= a[0], o[i][1] *= a[1], o[i][2] *= a[0], o[i][3] *= a[1];
+    const float ms0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
+    const float ms1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
+    const float p0 = ex2(lg[0] - ms0), p1 = ex2(lg[1] - ms1), p2 = ex2(lg[2] - ms0), p3 = ex2(lg[3] - ms1);
+    l_run[0] = l_run[0] * a[0] + p0 + p2;
+    l_run[1] = l_run[1] * a[1] + p1 + p3;
+    const uint32_t pb0 = movmatrix_trans(pack_bf162(p0, p1));
+    const uint32_t pb1 = movmatrix_trans(pack_bf162(p2, p3));
+#pragma unroll
+    for (int mv = 0; mv < 16; ++mv) {
+      uint32_t av[4];
+      const int tok = (lane & 7) + ((lane >> 4) << 3);
+      const int d = 16 * mv + ((lane >> 3) & 1) * 8;
+      ldmatrix_x4_trans(av, smem_u32(sv + tok * kDim + (((d >> 3) ^ (tok & 7)) << 3)));
+      mma_bf16_16816(o[mv], av[0], av[1], av[2], av[3], pb0, pb1);
+    }
+    __syncwarp();
+  }
+  // combine the 4 warps
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 4);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 8);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 16);
+  }
+  __syncthreads();
+  float *xch = reinterpret_cast<float *>(smem);  // [warp][64 + 4][32]
+  float *rec = xch + warp * (68 * 32);
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) rec[(i * 4 + q) * 32 + lane] = o[i][q];
+  rec[64 * 32 + lane] = m_run[0];
+  rec[65 * 32 + lane] = m_run[1];
+  rec[66 * 32 + lane] = l_run[0];
+  rec[67 * 32 + lane] = l_run[1];
+  __syncthreads();
+  if (warp != 0) return;
+  float M[2] = {-INFINITY, -INFINITY};
+  for (int w = 0; w < kRawWarps; ++w) {
+    M[0] = fmaxf(M[0], xch[w * 68 * 32 + 64 * 32 + lane]);
+    M[1] = fmaxf(M[1], xch[w * 68 * 32 + 65 * 32 + lane]);
+  }
+  float L[2] = {0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int w = 0; w < kRawWarps; ++w) {
+    const float *rw = xch + w * 68 * 32;
+    const float mw0 = rw[64 * 32 + lane], mw1 = rw[65 * 32 + lane];
+    const float e0 = mw0 == -INFINITY ? 0.f : ex2(mw0 - M[0]);
+    const float e1 = mw1 == -INFINITY ? 0.f : ex2(mw1 - M[1]);
+    L[0] = fmaf(e0, rw[66 * 32 + lane], L[0]);
+    L[1] = fmaf(e1, rw[67 * 32 + lane], L[1]);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[i][0] = fmaf(e0, rw[(i * 4 + 0) * 32 + lane], o[i][0]);
+      o[i][1] = fmaf(e1, rw[(i * 4 + 1) * 32 + lane], o[i][1]);
+      o[i][2] = fmaf(e0, rw[(i * 4 + 2) * 32 + lane], o[i][2]);
+      o[i][3] = fmaf(e1, rw[(i * 4 + 3) * 32 + lane], o[i][3]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = 8 * ntile + 2 * t + r;
+    if (row >= rows_valid) continue;
+    const int tok = ti.qstart + ti.qoff + row / g.group;
+    const int qh = head * g.group + row % g.group;
+    const int64_t orow = ((int64_t)tok * g.kv_heads * g.group + qh) * P.split_slots + P.split_index;
+    const bool any = L[r] > 0.f;
+    const float inv = any ? 1.0f / L[r] : 0.f;
+    float *dst = P.partials + orow * kDim;
+    // O^T fragment: m-tile mv rows (dims) 16mv + gi and 16mv + gi + 8
+#pragma unroll
+    for (int mv = 0; mv < 16; ++mv) {
+      dst[16 * mv + gi] = o[mv][r] * inv;
+      dst[16 * mv + gi + 8] = o[mv][2 + r] * inv;
+    }
+    if (gi == 0) P.lse[orow] = any ? (M[r] * 0.69314718055994531f + logf(L[r])) : -INFINITY;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// split merge (reference _merge_splits_kernel): warp per row
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) merge_splits_kernel(const float *__restrict__ partials,
+                                                           const float *__restrict__ lse, int64_t rows,
+                                                           int32_t hq, int32_t splits, int32_t slot_stride,
+                                                           const int32_t *__restrict__ counts,
+                                                           __nv_bfloat16 *__restrict__ out,
+                                                           float *__restrict__ logsum) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bool valid = row / hq < counts[1];
+  float m = -INFINITY;
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, valid ? lse[row * slot_stride + s] : -INFINITY);
+  const float safe = m == -INFINITY ? 0.f : m;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float den = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float l = valid ? lse[row * slot_stride + s] : -INFINITY;
+    const float w = expf(l - safe);
+    den += w;
+    if (w != 0.f) {
+      const float4 *src = reinterpret_cast<const float4 *>(partials + (row * slot_stride + s) * kDim + lane * 8);
+      const float4 x0 = src[0], x1 = src[1];
+      acc[0] = fmaf(w, x0.x, acc[0]), acc[1] = fmaf(w, x0.y, acc[1]), acc[2] = fmaf(w, x0.z, acc[2]);
+      acc[3] = fmaf(w, x0.w, acc[3]), acc[4] = fmaf(w, x1.x, acc[4]), acc[5] = fmaf(w, x1.y, acc[5]);
+      acc[6] = fmaf(w, x1.z, acc[6]), acc[7] = fmaf(w, x1.w, acc[7]);
+    }
+  }
+  const float inv = 1.0f / fmaxf(den, 1e-30f);
+  uint4 o;
+  o.x = pack_bf162(acc[0] * inv, acc[1] * inv);
+  o.y = pack_bf162(acc[2] * inv, acc[3] * inv);
+  o.z = pack_bf162(acc[4] * inv, acc[5] * inv);
+  o.w = pack_bf162(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4 *>(out + row * kDim + lane * 8) = o;
+  if (lane == 0) logsum[row] = den > 0.f ? m + logf(fmaxf(den, 1e-30f)) : -INFINITY;
+}
+
+// path merge (reference _merge_paths_kernel): warp per row
+__global__ void __launch_bounds__(256) merge_paths_kernel(const __nv_bfloat16 *__restrict__ a,
+                                                          const float *__restrict__ la,
+                                                          const float *__restrict__ b, int64_t b_stride,
+                                                          const float *__restrict__ lb, int64_t lb_stride,
+                                                          int64_t rows, int32_t hq,
+                                                          const int32_t *__restrict__ counts,
+                                                          __nv_bfloat16 *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bool valid = row / hq < counts[1];
+  const float xa = valid ? la[row] : -INFINITY;
+  const float xb = valid ? lb[row * lb_stride] : -INFINITY;
+  float m = fmaxf(xa, xb);
+  m = m == -INFINITY ? 0.f : m;
+  const float wa = expf(xa - m), wb = expf(xb - m);
+  const float inv = 1.0f / fmaxf(wa + wb, 1e-30f);
+  uint4 araw = valid ? *reinterpret_cast<const uint4 *>(a + row * kDim + lane * 8) : make_uint4(0, 0, 0, 0);
+  float4 b0 = make_float4(0, 0, 0, 0), b1 = b0;
+  if (valid && wb != 0.f) {
+    b0 = *reinterpret_cast<const float4 *>(b + row * b_stride + lane * 8);
+    b1 = *reinterpret_cast<const float4 *>(b + row * b_stride + lane * 8 + 4);
+  }
+  const uint32_t aw[4] = {araw.x, araw.y, araw.z, araw.w};
+  const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  uint32_t ow[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float r0 = (wa * bf16_bits_to_float(aw[i] & 0xffffu) + wb * bv[2 * i]) * inv;
+    const float r1 = (wa * bf16_bits_to_float(aw[i] >> 16) + wb * bv[2 * i + 1]) * inv;
+    ow[i] = pack_bf162(r0, r1);
+  }
+  *reinterpret_cast<uint4 *>(out + row * kDim + lane * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+// ----------------------------------------------------------------------------
+// fused epilogue of a decode step: split merge -> bf16 hrot -> hrot @ Rv^T (bf16
+// rounding, as the reference rotate) -> LSE path merge with the raw partial.
+// One CTA = 64 rows of [n*Hq]; the row-tile GEMM core does the inverse rotation.
+// ----------------------------------------------------------------------------
+struct FinalParams {
+  const float *partials, *lse;
+  int32_t split_slots, splits;
+  int64_t rows;
+  int32_t hq;
+  const int32_t *counts;
+  const __nv_bfloat16 *rv;
+  __nv_bfloat16 *out;
+};
+
+__global__ void __launch_bounds__(kGemmThreads) finalize_kernel(FinalParams P) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
+  __nv_bfloat16 *sB = sA + kAElems;
+  float *s_la = reinterpret_cast<float *>(sB + 2 * kBStageElems);  // [64]
+  float *s_lb = s_la + kTileRows;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row0 = (int64_t)blockIdx.x * kTileRows;
+  const int32_t active = P.counts[1];
+  for (int i = 0; i < kTileRows / 8; ++i) {
+    const int r = warp * 8 + i;
+    const int64_t row = row0 + r;
+    const bool valid = row < P.rows && row / P.hq < active;
+    float m = -INFINITY;
+    for (int s = 0; s < P.splits; ++s) m = fmaxf(m, valid ? P.lse[row * P.split_slots + s] : -INFINITY);
+    const float safe = m == -INFINITY ? 0.f : m;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float den = 0.f;
+    for (int s = 0; s < P.splits; ++s) {
+      const float l = valid ? P.lse[row * P.split_slots + s] : -INFINITY;
+      const float w = expf(l - safe);
+      den += w;
+      if (w != 0.f) {
+        const float4 *src = reinterpret_cast<const float4 *>(P.partials + (row * P.split_slots + s) * kDim + lane * 8);
+        const float4 x0 = src[0], x1 = src[1];
+        acc[0] = fmaf(w, x0.x, acc[0]), acc[1] = fmaf(w, x0.y, acc[1]), acc[2] = fmaf(w, x0.z, acc[2]);
+        acc[3] = fmaf(w, x0.w, acc[3]), acc[4] = fmaf(w, x1.x, acc[4]), acc[5] = fmaf(w, x1.y, acc[5]);
+        acc[6] = fmaf(w, x1.z, acc[6]), acc[7] = fmaf(w, x1.w, acc[7]);
+      }
+    }
+    const float inv = 1.0f / fmaxf(den, 1e-30f);
+    uint4 o;
+    o.x = pack_bf162(acc[0] * inv, acc[1] * inv);
+    o.y = pack_bf162(acc[2] * inv, acc[3] * inv);
+    o.z = pack_bf162(acc[4] * inv, acc[5] * inv);
+    o.w = pack_bf162(acc[6] * inv, acc[7] * inv);
+    *reinterpret_cast<uint4 *>(sA + r * kDim + ((lane ^ (r & 7)) << 3)) = o;
+    if (lane == 0) {
+      s_la[r] = den > 0.f ? m + logf(fmaxf(den, 1e-30f)) : -INFINITY;
+      s_lb[r] = valid ? P.lse[row * P.split_slots + P.splits] : -INFINITY;
+    }
+  }
+  float acc[2][8][4];
+  rowgemm_mainloop(acc, sA, sB, BMatrix{P.rv, 1, 256});  // B(k, n) = Rv[n][k]
+  const int wm = warp >> 2, wn = warp & 3, gq = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb) {
+      const int r = wm * 32 + mi * 16 + gq + 8 * hb;
+      const int64_t row = row0 + r;
+      if (row >= P.rows) continue;
+      const float xa = s_la[r], xb = s_lb[r];
+      float m = fmaxf(xa, xb);
+      m = m == -INFINITY ? 0.f : m;
+      const float wa = expf(xa - m), wb = expf(xb - m);
+      const float inv = 1.0f / fmaxf(wa + wb, 1e-30f);
+      const float *braw = P.partials + (row * P.split_slots + P.splits) * kDim;
+#pragma unroll
+      for (int nj = 0; nj < 8; ++nj) {
+        const int col = wn * 64 + nj * 8 + 2 * t;
+        // hout is rounded to bf16 (the reference rotate writes bf16)
+        const float h0 = bf16_bits_to_float(float_to_bf16_bits(acc[mi][nj][2 * hb]));
+        const float h1 = bf16_bits_to_float(float_to_bf16_bits(acc[mi][nj][2 * hb + 1]));
+        float b0 = 0.f, b1 = 0.f;
+        if (wb != 0.f) {
+          const float2 bb = *reinterpret_cast<const float2 *>(braw + col);
+          b0 = bb.x, b1 = bb.y;
+        }
+        const float r0 = (wa * h0 + wb * b0) * inv, r1 = (wa * h1 + wb * b1) * inv;
+        *reinterpret_cast<uint32_t *>(P.out + row * kDim + col) = pack_bf162(r0, r1);
+      }
+    }
+}
+
+// ----------------------------------------------------------------------------
+// window store (reference _window_store_kernel): CTA per request, warp per
+// (window index, head) pair, 16-byte lanes.
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) window_store_kernel(const __nv_bfloat16 *__restrict__ key,
+                                                           int64_t ks0, int64_t ks1,
+                                                           const __nv_bfloat16 *__restrict__ value,
+                                                           int64_t vs0, int64_t vs1,
+                                                           __nv_bfloat16 *__restrict__ window,
+                                                           const int32_t *__restrict__ qstarts,
+                                                           const int32_t *__restrict__ seq_lens,
+                                                           const int32_t *__restrict__ table,
+                                                           const int32_t *__restrict__ counts,
+                                                           oscar_geometry g) {
+  const int req = blockIdx.x;
+  if (req >= counts[0]) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qstart = qstarts[req];
+  const int qend = min(qstarts[req + 1], counts[1]);
+  const int seq = seq_lens[req];
+  const int prefix = seq - (qend - qstart);
+  if (qend <= qstart) return;
+  const int64_t owner = (int64_t)table[(int64_t)req * g.table_stride] / (g.block_tokens / kKernelBlock);
+  const int entries = (g.sink + g.ring) * g.kv_heads;
+  for (int e = warp; e < entries; e += 8) {
+    const int idx = e / g.kv_heads, head = e % g.kv_heads;
+    int pos;
+    if (idx < g.sink) {
+      pos = idx;
+    } else {
+      const int residue = idx - g.sink;
+      int mod = (seq - 1 - residue) % g.ring;
+      if (mod < 0) mod += g.ring;
+      pos = seq - 1 - mod;
+    }
+    const bool valid = pos >= prefix && pos < seq && (idx < g.sink || pos >= g.sink);
+    if (!valid) continue;
+    const int cur = qstart + pos - prefix;
+    const uint4 kv0 = *reinterpret_cast<const uint4 *>(key + (int64_t)cur * ks0 + (int64_t)head * ks1 + lane * 8);
+    const uint4 kv1 = *reinterpret_cast<const uint4 *>(value + (int64_t)cur * vs0 + (int64_t)head * vs1 + lane * 8);
+    *reinterpret_cast<uint4 *>(window + window_elem_offset(owner, idx, 0, head, g) + lane * 8) = kv0;
+    *reinterpret_cast<uint4 *>(window + window_elem_offset(owner, idx, 1, head, g) + lane * 8) = kv1;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// task table (reference _prepare_tasks_kernel): block 0 builds the table with a
+// block-wide scan; other blocks copy page-table columns.
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) prepare_tasks_kernel(const int32_t *__restrict__ qstarts,
+                                                             const int32_t *__restrict__ counts,
+                                                             int32_t *__restrict__ tasks,
+                                                             int32_t *__restrict__ task_count, int32_t capacity,
+                                                             int32_t query_tile, const int32_t *__restrict__ src,
+                                                             int64_t src_stride, int32_t *__restrict__ dst,
+                                                             int64_t dst_stride, int32_t copy_cols) {
+  const int nr = counts[0], active = counts[1];
+  if (blockIdx.x > 0) {
+    const int64_t total = (int64_t)nr * copy_cols;
+    for (int64_t i = (int64_t)(blockIdx.x - 1) * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)(gridDim.x - 1) * blockDim.x) {
+      const int64_t r = i / copy_cols, c = i % copy_cols;
+      dst[r * dst_stride + c] = src[r * src_stride + c];
+    }
+    return;
+  }
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < nr; base += blockDim.x) {
+    const int req = base + threadIdx.x;
+    int tiles = 0;
+    if (req < nr) {
+      const int s = min(qstarts[req], active), e = min(qstarts[req + 1], active);
+      tiles = (max(e - s, 0) + query_tile - 1) / query_tile;
+    }
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, ws, o);
+        if (lane >= o) ws += v;
+      }
+      warp_sums[lane] = ws;
+    }
+    __syncthreads();
+    const int excl = carry + (warp ? warp_sums[warp - 1] : 0) + incl - tiles;
+    for (int i = 0; i < tiles; ++i) {
+      const int slot = excl + i;
+      if (slot < capacity) {
+        tasks[2 * slot] = req;
+        tasks[2 * slot + 1] = i * query_tile;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_sums[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) task_count[0] = min(carry, capacity);
+}
+
+// ----------------------------------------------------------------------------
+// launch helpers
+// ----------------------------------------------------------------------------
+static bool geo_ok(const oscar_geometry &g) {
+  return g.head_dim == kDim && g.kv_heads > 0 && g.group > 0 && g.kernel_block == kKernelBlock &&
+         g.block_tokens % kKernelBlock == 0 && g.slot_bytes % 16 == 0 && g.vector_bytes == kDataBytes + 4 &&
+         g.page_bytes == (int64_t)g.block_tokens * g.kv_heads * kDim * 2 && g.ring > 0 && g.sink >= 0 &&
+         g.recent >= 0 && g.query_tile > 0 && g.table_stride > 0;
+}
+
+template <int MAXW>
+static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStream_t stream) {
+  static size_t configured = 0;
+  if (smem > configured) {
+    if (cudaFuncSetAttribute(history_attention_kernel<MAXW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return OSCAR_ERR_LAUNCH;
+    configured = smem;
+  }
+  history_attention_kernel<MAXW><<<grid, 32 * (P.consumers + 1), smem, stream>>>(P);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) {
+  const oscar_geometry &g = P.geo;
+  const int rows = g.query_tile * g.group;
+  P.ntiles = (rows + 7) / 8;
+  if (P.ntiles > kMaxConsumerWarps) return OSCAR_ERR_UNSUPPORTED;
+  int hpc = g.kv_heads;
+  while (hpc * P.ntiles > kMaxConsumerWarps) hpc = (hpc + 1) / 2;
+  if (g.kv_heads % hpc) hpc = 1;
+  P.heads_per_cta = hpc;
+  P.units = hpc * P.ntiles;
+  P.warps_per_unit = P.units >= 8 ? 1 : 8 / P.units;
+  P.consumers = P.units * P.warps_per_unit;
+  int ct = 128;
+  while (ct > 16 && ct * hpc * g.slot_bytes > 20480) ct >>= 1;
+  P.chunk_tokens = ct;
+  P.stage_bytes = ct * hpc * g.slot_bytes;
+  const size_t xch = ((size_t)(P.consumers - P.units) * (16 * 4 * 32 + 2 * 32) + (size_t)P.consumers * 4 * 32) * 4;
+  size_t smem = 128 + (size_t)kStages * P.stage_bytes;
+  if (smem < 128 + xch) smem = 128 + xch;
+  dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
+  if (P.consumers <= 8) return launch_history<8>(P, grid, smem, stream);
+  if (P.consumers <= 12) return launch_history<12>(P, grid, smem, stream);
+  return launch_history<16>(P, grid, smem, stream);
+}
+
+static int raw_launch(const RawParams &P, int32_t num_tasks, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(raw_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRawSmem) !=
+        cudaSuccess)
+      return OSCAR_ERR_LAUNCH;
+    configured = true;
+  }
+  dim3 grid(num_tasks, P.geo.kv_heads, P.ntiles);
+  raw_attention_kernel<<<grid, 32 * kRawWarps, kRawSmem, stream>>>(P);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+}  // namespace oscar
+
+using namespace oscar;
+
+extern "C" int oscar_prepare_tasks(const int32_t *qstarts, const int32_t *counts, int32_t *tasks,
+                                   int32_t *task_count, int32_t capacity, int32_t max_reqs, int32_t query_tile,
+                                   const int32_t *source_table, int64_t source_stride, int32_t *table,
+                                   int64_t table_stride, int32_t copy_columns, void *stream) {
+  if (!qstarts || !counts || !tasks || !task_count || capacity <= 0 || max_reqs <= 0 || query_tile <= 0)
+    return OSCAR_ERR_INVALID;
+  if (copy_columns > 0 && (!source_table || !table)) return OSCAR_ERR_INVALID;
+  int copy_blocks = 0;
+  if (copy_columns > 0) {
+    const int64_t total = (int64_t)max_reqs * copy_columns;
+    copy_blocks = (int)std::min<int64_t>((total + 1023) / 1024, 1024);
+  }
+  prepare_tasks_kernel<<<1 + copy_blocks, 1024, 0, (cudaStream_t)stream>>>(
+      qstarts, counts, tasks, task_count, capacity, query_tile, source_table, source_stride, table, table_stride,
+      copy_columns > 0 ? copy_columns : 0);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_attention_partials(const void *query, int64_t qs0, int64_t qs1, const void *key, int64_t ks0,
+                                        int64_t ks1, const void *value, int64_t vs0, int64_t vs1,
+                                        const uint8_t *history, const void *window, const int32_t *qstarts,
+                                        const int32_t *seq_lens, const int32_t *table, const int32_t *counts,
+                                        const int32_t *tasks, const int32_t *task_count, int32_t num_tasks,
+                                        int64_t n, float *partials, float *lse, oscar_geometry geo, float scale,
+                                        int32_t splits, int32_t raw, void *stream) {
+  if (!geo_ok(geo) || splits <= 0 || num_tasks < 0 || n < 0) return OSCAR_ERR_INVALID;
+  if (n == 0 || num_tasks == 0) return OSCAR_OK;
+  if (!query || !qstarts || !seq_lens || !table || !counts || !tasks || !task_count || !partials || !lse)
+    return OSCAR_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(query) & 15) || qs0 % 8 || qs1 % 8) return OSCAR_ERR_INVALID;
+  if (raw) {
+    if (splits != 1 || !key || !value || !window) return OSCAR_ERR_INVALID;
+    if (((reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value)) & 15) || ks0 % 8 || ks1 % 8 ||
+        vs0 % 8 || vs1 % 8)
+      return OSCAR_ERR_INVALID;
+    RawParams P{};
+    P.query = reinterpret_cast<const __nv_bfloat16 *>(query);
+    P.qs0 = qs0, P.qs1 = qs1;
+    P.key = reinterpret_cast<const __nv_bfloat16 *>(key);
+    P.value = reinterpret_cast<const __nv_bfloat16 *>(value);
+    P.ks0 = ks0, P.ks1 = ks1, P.vs0 = vs0, P.vs1 = vs1;
+    P.window = reinterpret_cast<const __nv_bfloat16 *>(window);
+    P.qstarts = qstarts, P.seq_lens = seq_lens, P.table = table, P.counts = counts;
+    P.tasks = tasks, P.task_count = task_count;
+    P.partials = partials, P.lse = lse, P.split_slots = 1, P.split_index = 0;
+    P.geo = geo;
+    P.scale_log2 = scale * kLog2e;
+    P.ntiles = (geo.query_tile * geo.group + 7) / 8;
+    return raw_launch(P, num_tasks, (cudaStream_t)stream);
+  }
+  if (!history) return OSCAR_ERR_INVALID;
+  HistParams P{};
+  P.query = reinterpret_cast<const __nv_bfloat16 *>(query);
+  P.qs0 = qs0, P.qs1 = qs1;
+  P.history = history;
+  P.qstarts = qstarts, P.seq_lens = seq_lens, P.table = table, P.counts = counts;
+  P.tasks = tasks, P.task_count = task_count, P.num_tasks = num_tasks;
+  P.partials = partials, P.lse = lse, P.split_slots = splits, P.splits = splits;
+  P.geo = geo;
+  P.scale_log2 = scale * kLog2e;
+  return history_launch(P, num_tasks, (cudaStream_t)stream);
+}
+
+extern "C" int oscar_merge_splits(const float *partials, const float *lse, int64_t n, int32_t hq, int32_t splits,
+                                  const int32_t *counts, void *out, float *logsum, void *stream) {
+  if (n < 0 || hq <= 0 || splits <= 0) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!partials || !lse || !counts || !out || !logsum) return OSCAR_ERR_INVALID;
+  const int64_t rows = n * hq;
+  merge_splits_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      partials, lse, rows, hq, splits, splits, counts, reinterpret_cast<__nv_bfloat16 *>(out), logsum);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_merge_paths(const void *a, const float *la, const float *b, int64_t b_row_stride,
+                                 const float *lb, int64_t lb_stride, int64_t n, int32_t hq, const int32_t *counts,
+                                 void *out, void *stream) {
+  if (n < 0 || hq <= 0) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!a || !la || !b || !lb || !counts || !out || b_row_stride % 4) return OSCAR_ERR_INVALID;
+  const int64_t rows = n * hq;
+  merge_paths_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(a), la, b, b_row_stride, lb, lb_stride, rows, hq, counts,
+      reinterpret_cast<__nv_bfloat16 *>(out));
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_store_windows(const void *key, int64_t ks0, int64_t ks1, const void *value, int64_t vs0,
+                                   int64_t vs1, void *window, const int32_t *qstarts, const int32_t *seq_lens,
+                                   const int32_t *table, const int32_t *counts, int32_t num_programs,
+                                   oscar_geometry geo, void *stream) {
+  if (!geo_ok(geo) || num_programs < 0) return OSCAR_ERR_INVALID;
+  if (num_programs == 0) return OSCAR_OK;
+  if (!key || !value || !window || !qstarts || !seq_lens || !table || !counts) return OSCAR_ERR_INVALID;
+  if (((reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value)) & 15) || ks0 % 8 || ks1 % 8 ||
+      vs0 % 8 || vs1 % 8)
+    return OSCAR_ERR_INVALID;
+  window_store_kernel<<<num_programs, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(key), ks0, ks1, reinterpret_cast<const __nv_bfloat16 *>(value), vs0,
+      vs1, reinterpret_cast<__nv_bfloat16 *>(window), qstarts, seq_lens, table, counts, geo);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64_t qs0, int64_t qs1, const void *key,
+                                      int64_t ks0, int64_t ks1, const void *value, int64_t vs0, int64_t vs1,
+                                      const uint8_t *history, void *window, const int32_t *qstarts,
+                                      const int32_t *seq_lens, const int32_t *table, const int32_t *counts,
+                                      const int32_t *tasks, const int32_t *task_count, int32_t num_tasks, int64_t n,
+                                      const void *rv, float *scratch_partials, float *scratch_lse, void *output,
+                                      oscar_geometry geo, float scale, int32_t splits, int32_t window_programs,
+                                      void *stream) {
+  if (!geo_ok(geo) || splits <= 0 || num_tasks < 0 || n < 0 || window_programs < 0) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!qrot || !query || !key || !value || !history || !window || !qstarts || !seq_lens || !table || !counts ||
+      !tasks || !task_count || !rv || !scratch_partials || !scratch_lse || !output)
+    return OSCAR_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(qrot) | reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key) |
+       reinterpret_cast<uintptr_t>(value) | reinterpret_cast<uintptr_t>(rv) | reinterpret_cast<uintptr_t>(output)) &
+      15)
+    return OSCAR_ERR_INVALID;
+  if (qs0 % 8 || qs1 % 8 || ks0 % 8 || ks1 % 8 || vs0 % 8 || vs1 % 8) return OSCAR_ERR_INVALID;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int hq = geo.kv_heads * geo.group;
+  if (num_tasks > 0) {
+    HistParams H{};
+    H.query = reinterpret_cast<const __nv_bfloat16 *>(qrot);
+    H.qs0 = (int64_t)hq * kDim, H.qs1 = kDim;  // qrot is contiguous [n, Hq, 256]
+    H.history = history;
+    H.qstarts = qstarts, H.seq_lens = seq_lens, H.table = table, H.counts = counts;
+    H.tasks = tasks, H.task_count = task_count, H.num_tasks = num_tasks;
+    H.partials = scratch_partials, H.lse = scratch_lse, H.split_slots = splits + 1, H.splits = splits;
+    H.geo = geo;
+    H.scale_log2 = scale * kLog2e;
+    int rc = history_launch(H, num_tasks, st);
+    if (rc) return rc;
+    RawParams R{};
+    R.query = reinterpret_cast<const __nv_bfloat16 *>(query);
+    R.qs0 = qs0, R.qs1 = qs1;
+    R.key = reinterpret_cast<const __nv_bfloat16 *>(key);
+    R.value = reinterpret_cast<const __nv_bfloat16 *>(value);
+    R.ks0 = ks0, R.ks1 = ks1, R.vs0 = vs0, R.vs1 = vs1;
+    R.window = reinterpret_cast<const __nv_bfloat16 *>(window);
+    R.qstarts = qstarts, R.seq_lens = seq_lens, R.table = table, R.counts = counts;
+    R.tasks = tasks, R.task_count = task_count;
+    R.partials = scratch_partials, R.lse = scratch_lse, R.split_slots = splits + 1, R.split_index = splits;
+    R.geo = geo;
+    R.scale_log2 = scale * kLog2e;
+    R.ntiles = (geo.query_tile * geo.group + 7) / 8;
+    rc = raw_launch(R, num_tasks, st);
+    if (rc) return rc;
+  }
+  static bool configured = false;
+  const int fsmem = kRowGemmSmem + 2 * kTileRows * 4;
+  if (!configured) {
+    if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fsmem) != cudaSuccess)
+      return OSCAR_ERR_LAUNCH;
+    configured = true;
+  }
+  FinalParams F{};
+  F.partials = scratch_partials, F.lse = scratch_lse, F.split_slots = splits + 1, F.splits = splits;
+  F.rows = n * hq, F.hq = hq, F.counts = counts;
+  F.rv = reinterpret_cast<const __nv_bfloat16 *>(rv);
+  F.out = reinterpret_cast<__nv_bfloat16 *>(output);
+  finalize_kernel<<<(unsigned)((F.rows + kTileRows - 1) / kTileRows), kGemmThreads, fsmem, st>>>(F);
+  OSCAR_CHECK_LAUNCH();
+  if (window_programs > 0) {
+    window_store_kernel<<<window_programs, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(key), ks0, ks1, reinterpret_cast<const __nv_bfloat16 *>(value), vs0,
+        vs1, reinterpret_cast<__nv_bfloat16 *>(window), qstarts, seq_lens, table, counts, geo);
+    OSCAR_CHECK_LAUNCH();
+  }
+  return OSCAR_OK;
+}

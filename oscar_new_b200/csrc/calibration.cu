@@ -1,0 +1,494 @@
+// OSCAR calibration on device: covariance Gram accumulation, SST weights,
+// normalisation and the batched symmetric eigensolver with U*H*P_br composition.
+// Reference: oscar_ascend/calibration_kernels.py:14-327.
+//
+// Eigensolver: the parallel cyclic (round-robin) Jacobi of the reference, with all
+// sweeps inside one launch.  A thread-block cluster of 8 CTAs owns one 256x256
+// matrix; CTA r holds rows [32r, 32r+32) of A and of U in shared memory (the column
+// rotations are row-local), and the row rotations exchange partner rows through
+// distributed shared memory.  Cluster barriers are hardware barriers (no software
+// spin), and the sweep count is bounded.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace oscar {
+
+// ----------------------------------------------------------------------------
+// Gram: cov[i][j] += sum_rows x[i] * x[j] (optionally * w_row).  CTA = 128 x 128
+// output tile (blockIdx.y in 0..3) over a chunk of rows (blockIdx.x); fp32 partial
+// tile reduced into cov with vector atomics.
+// ----------------------------------------------------------------------------
+constexpr int kGramRows = 32;     // rows per pipeline step
+constexpr int kGramChunk = 2048;  // rows per CTA
+
+__global__ void __launch_bounds__(256) gram_kernel(const __nv_bfloat16 *__restrict__ x, int64_t n, int32_t h,
+                                                   int64_t xs0, int64_t xs1, const float *__restrict__ w,
+                                                   float *__restrict__ cov) {
+  __shared__ __align__(16) __nv_bfloat16 si[kGramRows * 128];   // x[row][i-range]
+  __shared__ __align__(16) __nv_bfloat16 sj[kGramRows * 128];   // x[row][j-range] (or w*x hi)
+  __shared__ __align__(16) __nv_bfloat16 sjl[kGramRows * 128];  // w*x lo part
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ti = blockIdx.y >> 1, tj = blockIdx.y & 1;
+  const int64_t rows = n * h;
+  const int64_t r0 = (int64_t)blockIdx.x * kGramChunk;
+  const int64_t r1 = min(rows, r0 + kGramChunk);
+  const int wm = warp >> 2, wn = warp & 3;  // warp tile 64 (i) x 32 (j)
+  float acc[4][4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+  const bool weighted = w != nullptr;
+  for (int64_t rb = r0; rb < r1; rb += kGramRows) {
+    __syncthreads();
+    // 32 rows x 16 chunks (of 8 bf16) per side
+    for (int c = tid; c < kGramRows * 16; c += 256) {
+      const int r = c >> 4, ch = c & 15;
+      const int64_t row = rb + r;
+      uint4 vi = make_uint4(0, 0, 0, 0), vj = vi;
+      float wt = 0.f;
+      if (row < r1) {
+        const __nv_bfloat16 *src = x + (row / h) * xs0 + (row % h) * xs1;
+        vi = *reinterpret_cast<const uint4 *>(src + ti * 128 + ch * 8);
+        vj = *reinterpret_cast<const uint4 *>(src + tj * 128 + ch * 8);
+        if (weighted) wt = w[row];
+      }
+      const int sw = ((ch ^ (r & 7)) << 3);
+      *reinterpret_cast<uint4 *>(si + r * 128 + sw) = vi;
+      if (!weighted) {
+        *reinterpret_cast<uint4 *>(sj + r * 128 + sw) = vj;
+      } else {
+        const uint32_t vv[4] = {vj.x, vj.y, vj.z, vj.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float y0 = wt * bf16_bits_to_float(vv[e] & 0xffffu);
+          const float y1 = wt * bf16_bits_to_float(vv[e] >> 16);
+          hi[e] = pack_bf162(y0, y1);
+          lo[e] = pack_bf162(y0 - bf16_bits_to_float(hi[e] & 0xffffu), y1 - bf16_bits_to_float(hi[e] >> 16));
+        }
+        *reinterpret_cast<uint4 *>(sj + r * 128 + sw) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(sjl + r * 128 + sw) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kGramRows / 16; ++kk) {
+      // A = X^T (i x rows): stored [row][i] -> ldmatrix.trans
+      uint32_t a[4][4];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi) {
+        const int r = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int i = wm * 64 + mi * 16 + ((lane >> 3) & 1) * 8;
+        ldmatrix_x4_trans(a[mi], smem_u32(si + r * 128 + (((i >> 3) ^ (r & 7)) << 3)));
+      }
+#pragma unroll
+      for (int part = 0; part < (weighted ? 2 : 1); ++part) {
+        const __nv_bfloat16 *sb = part ? sjl : sj;
+        uint32_t b[4][2];
+#pragma unroll
+        for (int nj = 0; nj < 4; nj += 2) {
+          uint32_t t4[4];
+          const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int j = wn * 32 + (nj + (lane >> 4)) * 8;
+          ldmatrix_x4_trans(t4, smem_u32(sb + r * 128 + (((j >> 3) ^ (r & 7)) << 3)));
+          b[nj][0] = t4[0], b[nj][1] = t4[1], b[nj + 1][0] = t4[2], b[nj + 1][1] = t4[3];
+        }
+#pragma unroll
+        for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+          for (int nj = 0; nj < 4; ++nj)
+            mma_bf16_16816(acc[mi][nj], a[mi][0], a[mi][1], a[mi][2], a[mi][3], b[nj][0], b[nj][1]);
+      }
+    }
+  }
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int nj = 0; nj < 4; ++nj) {
+      const int i = ti * 128 + wm * 64 + mi * 16 + g;
+      const int j = tj * 128 + wn * 32 + nj * 8 + 2 * t;
+      atomicAdd(reinterpret_cast<float2 *>(cov + i * kDim + j), make_float2(acc[mi][nj][0], acc[mi][nj][1]));
+      atomicAdd(reinterpret_cast<float2 *>(cov + (i + 8) * kDim + j), make_float2(acc[mi][nj][2], acc[mi][nj][3]));
+    }
+}
+
+// ----------------------------------------------------------------------------
+// SST weights: w_t = max(k_t C k_t^T, 0); total += sum w.  CTA = 32 rows; thread j
+// owns column j of y = K C, fp32 FMAs (reference keeps this product in fp32).
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) sst_kernel(const __nv_bfloat16 *__restrict__ k, int64_t n, int32_t h,
+                                                  int64_t ks0, int64_t ks1, const float *__restrict__ c,
+                                                  float *__restrict__ w, float *__restrict__ total) {
+  __shared__ __align__(16) float sk[kDim][32];  // [i][row]
+  __shared__ float red[8][32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t rows = n * h;
+  const int64_t r0 = (int64_t)blockIdx.x * 32;
+  for (int e = tid; e < 32 * kDim; e += 256) {
+    const int r = e / kDim, i = e % kDim;
+    const int64_t row = r0 + r;
+    float v = 0.f;
+    if (row < rows) {
+      const uint16_t bits = reinterpret_cast<const uint16_t *>(k + (row / h) * ks0 + (row % h) * ks1)[i];
+      v = bf16_bits_to_float(bits);
+    }
+    sk[i][r] = v;
+  }
+  __syncthreads();
+  const int j = tid;
+  float y[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) y[r] = 0.f;
+  for (int i = 0; i < kDim; ++i) {
+    const float cij = c[i * kDim + j];
+    const float4 *kv = reinterpret_cast<const float4 *>(&sk[i][0]);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 kk = kv[q];
+      y[4 * q] = fmaf(kk.x, cij, y[4 * q]);
+      y[4 * q + 1] = fmaf(kk.y, cij, y[4 * q + 1]);
+      y[4 * q + 2] = fmaf(kk.z, cij, y[4 * q + 2]);
+      y[4 * q + 3] = fmaf(kk.w, cij, y[4 * q + 3]);
+    }
+  }
+  // w_r = sum_j y[r][j] * k[r][j]
+#pragma unroll
+  for (int r = 0; r < 32; ++r) {
+    float v = y[r] * sk[j][r];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp][r] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v += red[q][lane];
+    v = fmaxf(v, 0.f);
+    const bool ok = r0 + lane < rows;
+    if (ok) w[r0 + lane] = v;
+    float s = ok ? v : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) atomicAdd(total, s);
+  }
+}
+
+__global__ void normalize_kernel(const float *__restrict__ x, int64_t numel, const float *__restrict__ dden,
+                                 float hden, float *__restrict__ out) {
+  const float den = fmaxf(dden ? dden[0] : hden, 1e-30f);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = x[i] / den;
+}
+
+// ----------------------------------------------------------------------------
+// Jacobi eigensolver, one 8-CTA cluster per matrix
+// ----------------------------------------------------------------------------
+constexpr int kJCtas = 8;
+constexpr int kJRows = kDim / kJCtas;  // 32 rows per CTA
+constexpr int kJThreads = 256;
+
+struct JacobiSmem {
+  double a[kJRows][kDim];
+  double u[kJRows][kDim];
+  double tmp[kJRows][kDim];
+  double cs[kDim / 2][2];
+  double diag[kDim];
+  double stat[2];
+  int flag[2];
+};
+
+OSCAR_DEVINL void round_pair(int j, int r, int &p, int &q) {
+  if (j == 0) {
+    p = kDim - 1;
+    q = r;
+  } else {
+    p = (r + j) % (kDim - 1);
+    q = (r - j + kDim - 1) % (kDim - 1);
+  }
+}
+
+// The arithmetic is carried in fp64 (the reference uses fp32): same rotations, skip rule
+// and stopping rule, but eigenvalues accurate to the fp32 input.
+__global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__restrict__ cov, int32_t max_sweeps,
+                                                             float tol, float *__restrict__ rot,
+                                                             float *__restrict__ evals, float *__restrict__ info) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  JacobiSmem &S = *reinterpret_cast<JacobiSmem *>(smem_raw);
+  __shared__ double wo[8], wd[8];
+  __shared__ int wf[8];
+  __shared__ int rank_of[kDim];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int batch = blockIdx.x / kJCtas;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float *C = cov + (size_t)batch * kDim * kDim;
+  const int row0 = rank * kJRows;
+  for (int e = tid; e < kJRows * kDim; e += kJThreads) {
+    const int r = e / kDim, c = e % kDim;
+    const int gr = row0 + r;
+    S.a[r][c] = ((double)C[gr * kDim + c] + (double)C[c * kDim + gr]) * 0.5;
+    S.u[r][c] = gr == c ? 1.0 : 0.0;
+  }
+  cluster.sync();
+  double residual = INFINITY;
+  int sweeps_done = 0;
+  bool finite = true;
+  for (int sweep = 0; sweep < max_sweeps; ++sweep) {
+    for (int r = 0; r < kDim - 1; ++r) {
+      // (1) rotation parameters of the pairs whose p-row is local, pushed to all CTAs
+      if (tid < kDim / 2) {
+        int p, q;
+        round_pair(tid, r, p, q);
+        if (p / kJRows == rank) {
+          const double app = S.a[p - row0][p];
+          const double apq = S.a[p - row0][q];
+          const JacobiSmem *owner_q = cluster.map_shared_rank(&S, q / kJRows);
+          const double aqq = owner_q->a[q % kJRows][q];
+          const double delta = (aqq - app) * 0.5;
+          const double sgn = delta >= 0.0 ? 1.0 : -1.0;
+          double tang = sgn * apq / fmax(fabs(delta) + sqrt(delta * delta + apq * apq), 1e-30);
+          if (!(fabs(apq) > 1e-8 * (fabs(app) + fabs(aqq)) + 1e-20)) tang = 0.0;
+          const double cs = 1.0 / sqrt(1.0 + tang * tang);
+          const double sn = tang * cs;
+          for (int dst = 0; dst < kJCtas; ++dst) {
+            JacobiSmem *o = cluster.map_shared_rank(&S, dst);
+            o->cs[tid][0] = cs;
+            o->cs[tid][1] = sn;
+          }
+        }
+      }
+      cluster.sync();
+      // (2) column rotations of the local rows of A and U
+      for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
+        const int lr = e / (kDim / 2), j = e % (kDim / 2);
+        int p, q;
+        round_pair(j, r, p, q);
+        const double c = S.cs[j][0], s = S.cs[j][1];
+        const double ap = S.a[lr][p], aq = S.a[lr][q];
+        S.a[lr][p] = ap * c - aq * s;
+        S.a[lr][q] = ap * s + aq * c;
+        const double up = S.u[lr][p], uq = S.u[lr][q];
+        S.u[lr][p] = up * c - uq * s;
+        S.u[lr][q] = up * s + uq * c;
+      }
+      cluster.sync();
+      // (3) fetch each local row's partner row (possibly remote), then (4) row rotations
+      for (int e = tid; e < kJRows * kDim; e += kJThreads) {
+        const int lr = e / kDim, col = e % kDim;
+        const int x = row0 + lr;
+        int y;
+        if (x == kDim - 1) y = r;
+        else if (x == r) y = kDim - 1;
+        else y = ((2 * r - x) % (kDim - 1) + (kDim - 1)) % (kDim - 1);
+        const JacobiSmem *own = cluster.map_shared_rank(&S, y / kJRows);
+        S.tmp[lr][col] = own->a[y % kJRows][col];
+      }
+      cluster.sync();
+      for (int e = tid; e < kJRows * kDim; e += kJThreads) {
+        const int lr = e / kDim, col = e % kDim;
+        const int x = row0 + lr;
+        int j, isp;
+        if (x == kDim - 1) {
+          j = 0, isp = 1;
+        } else if (x == r) {
+          j = 0, isp = 0;
+        } else {
+          const int jp = ((x - r) % (kDim - 1) + (kDim - 1)) % (kDim - 1);  // x = (r + jp) mod (D-1)
+          if (jp >= 1 && jp < kDim / 2) {
+            j = jp, isp = 1;
+          } else {
+            j = ((r - x) % (kDim - 1) + (kDim - 1)) % (kDim - 1), isp = 0;  // x = (r - j) mod (D-1)
+          }
+        }
+        const double c = S.cs[j][0], s = S.cs[j][1];
+        const double bx = S.a[lr][col], by = S.tmp[lr][col];
+        S.a[lr][col] = isp ? (c * bx - s * by) : (s * by + c * bx);
+      }
+      cluster.sync();
+    }
+    sweeps_done = sweep + 1;
+    if ((sweep + 1) % 2 == 0 || sweep + 1 == max_sweeps) {
+      // residual = max|offdiag| / max|diag| over the matrix (non-finite -> fail)
+      double off = 0.0, dg = 0.0;
+      bool fin = true;
+      for (int e = tid; e < kJRows * kDim; e += kJThreads) {
+        const int lr = e / kDim, col = e % kDim;
+        const double v = S.a[lr][col];
+        if (!isfinite(v)) fin = false;
+        if (col == row0 + lr) dg = fmax(dg, fabs(v));
+        else off = fmax(off, fabs(v));
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        off = fmax(off, __shfl_xor_sync(0xffffffffu, off, o));
+        dg = fmax(dg, __shfl_xor_sync(0xffffffffu, dg, o));
+      }
+      fin = __all_sync(0xffffffffu, fin);
+      if (lane == 0) wo[warp] = off, wd[warp] = dg, wf[warp] = fin;
+      __syncthreads();
+      if (tid == 0) {
+        double o = 0.0, d = 0.0;
+        int f = 1;
+        for (int q = 0; q < 8; ++q) o = fmax(o, wo[q]), d = fmax(d, wd[q]), f &= wf[q];
+        S.stat[0] = o, S.stat[1] = d, S.flag[0] = f;
+      }
+      cluster.sync();
+      double o = 0.0, d = 0.0;
+      int f = 1;
+      for (int q = 0; q < kJCtas; ++q) {
+        const JacobiSmem *other = cluster.map_shared_rank(&S, q);
+        o = fmax(o, other->stat[0]);
+        d = fmax(d, other->stat[1]);
+        f &= other->flag[0];
+      }
+      finite = f != 0 && isfinite(o) && isfinite(d);
+      residual = finite ? o / fmax(d, 1e-30) : INFINITY;
+      cluster.sync();
+      if (!finite || residual < (double)tol) break;
+    }
+  }
+  // eigenvalues: gather the diagonal, rank ascending (ties by index)
+  if (tid < kJRows) S.tmp[0][row0 + tid] = S.a[tid][row0 + tid];
+  cluster.sync();
+  for (int i = tid; i < kDim; i += kJThreads) {
+    const JacobiSmem *own = cluster.map_shared_rank(&S, i / kJRows);
+    S.diag[i] = own->tmp[0][i];
+  }
+  cluster.sync();
+  for (int i = tid; i < kDim; i += kJThreads) {
+    const double v = S.diag[i];
+    int rk = 0;
+    for (int k2 = 0; k2 < kDim; ++k2) {
+      const double o = S.diag[k2];
+      rk += (o < v) || (o == v && k2 < i);
+    }
+    rank_of[i] = rk;
+    if (rank == 0) evals[(size_t)batch * kDim + rk] = (float)v;
+  }
+  __syncthreads();
+  // sorted U rows (local), Hadamard butterfly, bit-reversed placement, / sqrt(256)
+  for (int e = tid; e < kJRows * kDim; e += kJThreads) {
+    const int lr = e / kDim, i = e % kDim;
+    S.tmp[lr][rank_of[i]] = S.u[lr][i];
+  }
+  __syncthreads();
+  for (int lr = warp; lr < kJRows; lr += 8) {
+    double v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = S.tmp[lr][8 * lane + e];
+#pragma unroll
+    for (int bit = 0; bit < 3; ++bit) {
+      double nv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const double partner = v[e ^ (1 << bit)];
+        nv[e] = (e & (1 << bit)) ? partner - v[e] : v[e] + partner;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = nv[e];
+    }
+#pragma unroll
+    for (int bit = 3; bit < 8; ++bit) {
+      const int lm = 1 << (bit - 3);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const double partner = __shfl_xor_sync(0xffffffffu, v[e], lm);
+        v[e] = (lane & lm) ? partner - v[e] : v[e] + partner;
+      }
+    }
+    float *dst = rot + ((size_t)batch * kDim + row0 + lr) * kDim;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = 8 * lane + e;
+      const int rev = __brev((unsigned)(kDim - 1 - i)) >> 24;
+      dst[rev] = (float)(v[e] * 0.0625);
+    }
+  }
+  if (rank == 0 && tid == 0) {
+    float *inf4 = info + (size_t)batch * 4;
+    inf4[0] = (float)sweeps_done;
+    inf4[1] = (float)residual;
+    inf4[2] = !finite ? 2.f : (residual < (double)tol ? 0.f : 1.f);
+    inf4[3] = 0.f;
+  }
+  cluster.sync();  // keep shared memory alive until every remote read is done
+}
+
+}  // namespace oscar
+
+using namespace oscar;
+
+extern "C" int oscar_accumulate_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1,
+                                     const float *weights, float *cov, void *stream) {
+  if (n < 0 || h <= 0 || !cov) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!x || (reinterpret_cast<uintptr_t>(x) & 15) || xs0 % 8 || xs1 % 8) return OSCAR_ERR_INVALID;
+  const int64_t rows = n * h;
+  dim3 grid((unsigned)((rows + kGramChunk - 1) / kGramChunk), 4);
+  gram_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16 *>(x), n, h, xs0, xs1,
+                                                      weights, cov);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_sst_weights(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1, const float *q_cov,
+                                 float *weights, float *total, void *stream) {
+  if (n < 0 || h <= 0 || !q_cov || !weights || !total) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!key) return OSCAR_ERR_INVALID;
+  const int64_t rows = n * h;
+  sst_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(key), n, h, ks0, ks1, q_cov, weights, total);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_normalize(const float *x, int64_t numel, const float *device_denominator, float host_denominator,
+                               float *out, void *stream) {
+  if (numel < 0 || !x || !out) return OSCAR_ERR_INVALID;
+  if (numel == 0) return OSCAR_OK;
+  const unsigned blocks = (unsigned)std::min<int64_t>((numel + 255) / 256, 4096);
+  normalize_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(x, numel, device_denominator, host_denominator, out);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_jacobi_rotations(const float *cov, int32_t batch, int32_t max_sweeps, float tolerance,
+                                      float *rotations, float *eigenvalues, float *info, void *stream) {
+  if (batch < 0 || max_sweeps <= 0 || max_sweeps > 64 || !(tolerance > 0.f)) return OSCAR_ERR_INVALID;
+  if (batch == 0) return OSCAR_OK;
+  if (!cov || !rotations || !eigenvalues || !info) return OSCAR_ERR_INVALID;
+  const int smem = (int)sizeof(JacobiSmem);
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return OSCAR_ERR_LAUNCH;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kJCtas * batch);
+  cfg.blockDim = dim3(kJThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kJCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, jacobi_kernel, cov, max_sweeps, tolerance, rotations, eigenvalues, info) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return OSCAR_ERR_LAUNCH;
+  }
+  return OSCAR_OK;
+}

@@ -1,0 +1,278 @@
+// Rotation GEMM, INT2 clip/pack/scatter store (standalone and fused), unpack.
+//
+// Reference: oscar_ascend/kernels.py:14-66 (rotate), :69-202 (clip, store_int2),
+// :623-672 (unpack / dequant_inverse_rotate).
+#include "quant.cuh"
+#include "rowgemm.cuh"
+
+namespace oscar {
+
+// ----------------------------------------------------------------------------
+// standalone store: one warp per (token, head) row, K then V
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) store_int2_kernel(const __nv_bfloat16 *__restrict__ krot,
+                                                         const __nv_bfloat16 *__restrict__ vrot,
+                                                         int64_t rows, uint8_t *__restrict__ history,
+                                                         const int64_t *__restrict__ slots,
+                                                         const int32_t *__restrict__ counts,
+                                                         oscar_geometry geo, oscar_clip kc, oscar_clip vc) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t token = row / geo.kv_heads;
+  const int head = (int)(row % geo.kv_heads);
+  if (token >= counts[1]) return;
+  const int64_t slot = slots[token];
+  if (slot < 0) return;
+  uint8_t *dst = history + slot_byte_offset(slot, head, geo);
+#pragma unroll 1
+  for (int kv = 0; kv < 2; ++kv) {
+    const __nv_bfloat16 *src = (kv == 0 ? krot : vrot) + row * kDim + lane * 8;
+    const uint4 raw = *reinterpret_cast<const uint4 *>(src);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = bf16_bits_to_float(w[i] & 0xffffu);
+      x[2 * i + 1] = bf16_bits_to_float(w[i] >> 16);
+    }
+    quantize_pack_warp(x, kv == 0 ? kc : vc, dst + kv * geo.vector_bytes, true);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// rotation GEMM (+ optional fused quantise/store epilogue)
+// ----------------------------------------------------------------------------
+struct RotateJob {
+  const __nv_bfloat16 *x;  // rows (t, h) at x + t*s0 + h*s1, unit inner stride
+  int64_t s0, s1;
+  int64_t n;               // tokens
+  int32_t h;               // heads per token
+  BMatrix r;
+  __nv_bfloat16 *y;        // contiguous [n*h, 256] output (nullable for store jobs)
+  int32_t kv;              // -1: plain rotate, 0: K store, 1: V store
+  int64_t tiles;
+};
+
+struct RotateParams {
+  RotateJob job[3];
+  int32_t njobs;
+  uint8_t *history;
+  const int64_t *slots;
+  const int32_t *counts;
+  oscar_geometry geo;
+  oscar_clip clip[2];
+};
+
+__global__ void __launch_bounds__(kGemmThreads) rotate_kernel(RotateParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
+  __nv_bfloat16 *sB = sA + kAElems;
+  int64_t tile = blockIdx.x;
+  int j = 0;
+  while (j < p.njobs - 1 && tile >= p.job[j].tiles) {
+    tile -= p.job[j].tiles;
+    ++j;
+  }
+  const RotateJob job = p.job[j];
+  const int64_t nrows = job.n * job.h;
+  const int64_t row0 = tile * kTileRows;
+  load_a_tile(sA, row0, nrows, [&](int64_t r) {
+    return job.x + (r / job.h) * job.s0 + (r % job.h) * job.s1;
+  });
+  cp_async_commit();
+  float acc[2][8][4];
+  rowgemm_mainloop(acc, sA, sB, job.r);
+  // acc -> bf16 tile (rounded exactly once, as the reference rotate output)
+  store_acc_bf16(sA, acc);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (job.kv < 0 || job.y != nullptr) {
+    // copy the bf16 tile out: 64 rows x 32 chunks
+    for (int c = threadIdx.x; c < kTileRows * 32; c += kGemmThreads) {
+      const int r = c >> 5, ch = c & 31;
+      if (row0 + r < nrows)
+        *reinterpret_cast<uint4 *>(job.y + (row0 + r) * kDim + ch * 8) =
+            *reinterpret_cast<const uint4 *>(sA + r * kDim + ((ch ^ (r & 7)) << 3));
+    }
+  }
+  if (job.kv < 0) return;
+  const int32_t active = p.counts[1];
+#pragma unroll 1
+  for (int i = 0; i < kTileRows / 8; ++i) {
+    const int r = warp * (kTileRows / 8) + i;
+    const int64_t row = row0 + r;
+    if (row >= nrows) break;  // warp-uniform
+    const int64_t token = row / job.h;
+    const int head = (int)(row % job.h);
+    const int64_t slot = token < active ? p.slots[token] : -1;
+    if (slot < 0) continue;  // warp-uniform
+    const uint4 raw = *reinterpret_cast<const uint4 *>(sA + r * kDim + (((lane) ^ (r & 7)) << 3));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    float x[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      x[2 * q] = bf16_bits_to_float(w[q] & 0xffffu);
+      x[2 * q + 1] = bf16_bits_to_float(w[q] >> 16);
+    }
+    uint8_t *dst = p.history + slot_byte_offset(slot, head, p.geo) + job.kv * p.geo.vector_bytes;
+    quantize_pack_warp(x, p.clip[job.kv], dst, true);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// diagnostic unpack (reference _unpack_kernel): warp per (token, head)
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) unpack_kernel(const uint8_t *__restrict__ history,
+                                                     const int64_t *__restrict__ slots, int64_t n,
+                                                     oscar_geometry geo, __nv_bfloat16 *__restrict__ kout,
+                                                     __nv_bfloat16 *__restrict__ vout) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= n * geo.kv_heads) return;
+  const int64_t token = row / geo.kv_heads;
+  const int head = (int)(row % geo.kv_heads);
+  const int64_t slot = slots[token];
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    uint32_t out[4] = {0, 0, 0, 0};
+    if (slot >= 0) {
+      const uint8_t *src = history + slot_byte_offset(slot, head, geo) + kv * geo.vector_bytes;
+      const uint32_t codes = reinterpret_cast<const uint16_t *>(src)[lane];
+      const uint32_t sz = *reinterpret_cast<const uint32_t *>(src + kDataBytes);
+      const float s = half_bits_to_float(sz & 0xffffu), z = half_bits_to_float(sz >> 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float c0 = (float)((codes >> (4 * i)) & 3u), c1 = (float)((codes >> (4 * i + 2)) & 3u);
+        out[i] = pack_bf162(__fadd_rn(__fmul_rn(c0, s), z), __fadd_rn(__fmul_rn(c1, s), z));
+      }
+    }
+    __nv_bfloat16 *dst = (kv == 0 ? kout : vout) + row * kDim + lane * 8;
+    *reinterpret_cast<uint4 *>(dst) = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+static bool rotation_ok(const void *r, int64_t rs0, int64_t rs1) {
+  if (!r) return false;
+  if (!((rs1 == 1 && rs0 % 8 == 0) || (rs0 == 1 && rs1 % 8 == 0))) return false;
+  return (reinterpret_cast<uintptr_t>(r) & 15) == 0;
+}
+
+static bool rows_ok(const void *x, int64_t s0, int64_t s1) {
+  return x && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && s0 % 8 == 0 && s1 % 8 == 0;
+}
+
+static bool geometry_ok(const oscar_geometry &g) {
+  return g.head_dim == kDim && g.kv_heads > 0 && g.block_tokens > 0 && g.kernel_block == kKernelBlock &&
+         g.block_tokens % kKernelBlock == 0 && g.slot_bytes % 16 == 0 && g.slot_bytes >= 2 * g.vector_bytes &&
+         g.vector_bytes == kDataBytes + 4 && g.page_bytes == (int64_t)g.block_tokens * g.kv_heads * kDim * 2;
+}
+
+static bool clip_ok(const oscar_clip &c) {
+  if (!c.enabled) return true;
+  if (c.mode == 1) return c.factor > 0.f && c.factor <= 1.f;
+  return c.mode == 0 && c.asc_lo >= 0 && c.asc_hi <= 255 && c.asc_lo <= c.asc_hi && c.asc_hi - c.asc_lo <= 1 &&
+         c.weight >= 0.f && c.weight < 1.f;
+}
+
+static int set_smem_once() {
+  static bool done = false;
+  if (!done) {
+    if (cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowGemmSmem) !=
+        cudaSuccess)
+      return OSCAR_ERR_LAUNCH;
+    done = true;
+  }
+  return OSCAR_OK;
+}
+
+}  // namespace oscar
+
+using namespace oscar;
+
+extern "C" int oscar_version(void) { return 100; }
+
+extern "C" int oscar_rotate(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int64_t xs2,
+                            const void *r, int64_t rs0, int64_t rs1, void *y, void *stream) {
+  if (n < 0 || h <= 0 || xs2 != 1 || !y) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!rows_ok(x, xs0, xs1) || !rotation_ok(r, rs0, rs1)) return OSCAR_ERR_INVALID;
+  if (set_smem_once() != OSCAR_OK) return OSCAR_ERR_LAUNCH;
+  RotateParams p{};
+  p.njobs = 1;
+  p.job[0] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(x), xs0, xs1, n, h,
+                       BMatrix{reinterpret_cast<const __nv_bfloat16 *>(r), rs0, rs1},
+                       reinterpret_cast<__nv_bfloat16 *>(y), -1, (n * h + kTileRows - 1) / kTileRows};
+  rotate_kernel<<<(unsigned)p.job[0].tiles, kGemmThreads, kRowGemmSmem, (cudaStream_t)stream>>>(p);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_store_int2(const void *krot, const void *vrot, int64_t n, void *history,
+                                const int64_t *slots, const int32_t *counts, oscar_geometry geo,
+                                oscar_clip kclip, oscar_clip vclip, void *stream) {
+  if (n < 0 || !geometry_ok(geo) || !clip_ok(kclip) || !clip_ok(vclip)) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!krot || !vrot || !history || !slots || !counts) return OSCAR_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(krot) | reinterpret_cast<uintptr_t>(vrot)) & 15) return OSCAR_ERR_INVALID;
+  const int64_t rows = n * geo.kv_heads;
+  store_int2_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(krot), reinterpret_cast<const __nv_bfloat16 *>(vrot), rows,
+      reinterpret_cast<uint8_t *>(history), slots, counts, geo, kclip, vclip);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_rotate_store(const void *key, int64_t ks0, int64_t ks1, const void *value, int64_t vs0,
+                                  int64_t vs1, int64_t n, const void *rk, const void *rv, void *history,
+                                  const int64_t *slots, const int32_t *counts, oscar_geometry geo,
+                                  oscar_clip kclip, oscar_clip vclip, const void *query, int64_t qs0,
+                                  int64_t qs1, int32_t hq, void *qrot_out, void *krot_out, void *vrot_out,
+                                  void *stream) {
+  if (n < 0 || !geometry_ok(geo) || !clip_ok(kclip) || !clip_ok(vclip)) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!history || !slots || !counts) return OSCAR_ERR_INVALID;
+  if (!rows_ok(key, ks0, ks1) || !rows_ok(value, vs0, vs1)) return OSCAR_ERR_INVALID;
+  if (!rotation_ok(rk, 256, 1) || !rotation_ok(rv, 256, 1)) return OSCAR_ERR_INVALID;
+  if (query && (!rows_ok(query, qs0, qs1) || hq <= 0 || !qrot_out)) return OSCAR_ERR_INVALID;
+  if (set_smem_once() != OSCAR_OK) return OSCAR_ERR_LAUNCH;
+  const int64_t tiles = (n * geo.kv_heads + kTileRows - 1) / kTileRows;
+  RotateParams p{};
+  p.history = reinterpret_cast<uint8_t *>(history);
+  p.slots = slots;
+  p.counts = counts;
+  p.geo = geo;
+  p.clip[0] = kclip;
+  p.clip[1] = vclip;
+  p.job[0] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(key), ks0, ks1, n, geo.kv_heads,
+                       BMatrix{reinterpret_cast<const __nv_bfloat16 *>(rk), 256, 1},
+                       reinterpret_cast<__nv_bfloat16 *>(krot_out), 0, tiles};
+  p.job[1] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(value), vs0, vs1, n, geo.kv_heads,
+                       BMatrix{reinterpret_cast<const __nv_bfloat16 *>(rv), 256, 1},
+                       reinterpret_cast<__nv_bfloat16 *>(vrot_out), 1, tiles};
+  p.njobs = 2;
+  int64_t total = 2 * tiles;
+  if (query) {
+    const int64_t qt = (n * hq + kTileRows - 1) / kTileRows;
+    p.job[2] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(query), qs0, qs1, n, hq,
+                         BMatrix{reinterpret_cast<const __nv_bfloat16 *>(rk), 256, 1},
+                         reinterpret_cast<__nv_bfloat16 *>(qrot_out), -1, qt};
+    p.njobs = 3;
+    total += qt;
+  }
+  rotate_kernel<<<(unsigned)total, kGemmThreads, kRowGemmSmem, (cudaStream_t)stream>>>(p);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_unpack(const uint8_t *history, const int64_t *slots, int64_t n, oscar_geometry geo,
+                            void *k_out, void *v_out, void *stream) {
+  if (n < 0 || !geometry_ok(geo)) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!history || !slots || !k_out || !v_out) return OSCAR_ERR_INVALID;
+  const int64_t rows = n * geo.kv_heads;
+  unpack_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      history, slots, n, geo, reinterpret_cast<__nv_bfloat16 *>(k_out), reinterpret_cast<__nv_bfloat16 *>(v_out));
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}

@@ -1,0 +1,291 @@
+"""OSCAR INT2 KV-cache operators on B200, behind the reference's operator names.
+
+Each function keeps the name, argument order and meaning of the reference's
+``oscar_ascend/kernels.py`` (Triton-Ascend) and calls the sm_100a CUDA library through
+its C ABI.  There is deliberately no CPU fallback: tensors must live on a CUDA device
+and the library must be built, otherwise the call raises.
+
+Fused entry points that the reference does not have (``rotate_store``,
+``decode_attention``) implement the same arithmetic in fewer launches; the backend
+uses them.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from .config import attention_programs, quantile_weight_f32
+
+LOG2E = 1.4426950408889634
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("OSCAR kernels run on a CUDA device only (no CPU fallback)")
+
+
+def _rows(x: torch.Tensor):
+    """[n, h, 256] bf16 view with unit inner stride and 16-byte aligned rows."""
+    if x.dtype != torch.bfloat16 or x.ndim != 3 or x.shape[-1] != 256:
+        raise ValueError(f"expected bf16 [n, h, 256], got {tuple(x.shape)} {x.dtype}")
+    if x.stride(2) != 1 or x.stride(0) % 8 or x.stride(1) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    return x
+
+
+def geometry(layout, hq: int, table_stride: int) -> _lib.Geometry:
+    cfg = layout.config
+    if hq % layout.kv_heads:
+        raise ValueError("query heads must be a multiple of KV heads")
+    return _lib.Geometry(
+        kv_heads=layout.kv_heads,
+        group=hq // layout.kv_heads,
+        head_dim=cfg.head_dim,
+        block_tokens=layout.physical_block_tokens,
+        kernel_block=layout.kernel_block_tokens,
+        slot_bytes=cfg.slot_bytes,
+        vector_bytes=cfg.vector_bytes,
+        sink=cfg.sink_tokens,
+        recent=cfg.recent_tokens,
+        ring=cfg.ring_tokens,
+        table_stride=table_stride,
+        query_tile=cfg.queries_per_tile,
+        page_bytes=layout.stripe_page_bytes,
+    )
+
+
+def clip_params(cfg, kind: str) -> _lib.Clip:
+    """torch.quantile semantics (fp32 rank/weight) or fixed max-abs factor."""
+    ratio = cfg.k_clip_ratio if kind == "k" else cfg.v_clip_ratio
+    factor = cfg.k_clip_factor if kind == "k" else cfg.v_clip_factor
+    if cfg.clip_mode == "factor":
+        return _lib.Clip(enabled=1, mode=1, asc_lo=0, asc_hi=0, weight=0.0, factor=factor)
+    if not ratio:
+        return _lib.Clip(enabled=0, mode=0, asc_lo=0, asc_hi=0, weight=0.0, factor=1.0)
+    lo, hi, w = quantile_weight_f32(ratio, cfg.head_dim)
+    return _lib.Clip(enabled=1, mode=0, asc_lo=lo, asc_hi=hi, weight=w, factor=1.0)
+
+
+def _rotation(r: torch.Tensor):
+    if r.dtype != torch.bfloat16 or r.shape != (256, 256):
+        raise ValueError("rotation must be bf16 [256, 256]")
+    s0, s1 = r.stride()
+    if not ((s1 == 1 and s0 % 8 == 0) or (s0 == 1 and s1 % 8 == 0)) or r.data_ptr() % 16:
+        r = r.contiguous()
+    return r
+
+
+# ----------------------------------------------------------------------------
+# reference operators (oscar_ascend/kernels.py)
+# ----------------------------------------------------------------------------
+
+
+def rotate(x: torch.Tensor, rotation: torch.Tensor) -> torch.Tensor:
+    """``bf16(x) @ bf16(R)`` with fp32 accumulation -> bf16 (reference kernels.py:51-66)."""
+    _require_cuda(x, rotation)
+    n, h, d = x.shape
+    out = torch.empty((n, h, d), device=x.device, dtype=torch.bfloat16)
+    if n == 0:
+        return out
+    x = _rows(x)
+    r = _rotation(rotation)
+    _lib.call("oscar_rotate", x.data_ptr(), n, h, x.stride(0), x.stride(1), x.stride(2), r.data_ptr(),
+              r.stride(0), r.stride(1), out.data_ptr(), _stream(x))
+    return out
+
+
+def store_int2(key_rot, value_rot, history, slots, counts, layout):
+    """Clip + INT2 pack + masked scatter (reference kernels.py:175-202)."""
+    _require_cuda(key_rot, value_rot, history, slots, counts)
+    cfg = layout.config
+    n = key_rot.shape[0]
+    kr, vr = key_rot.contiguous(), value_rot.contiguous()
+    geo = geometry(layout, layout.kv_heads, 1)
+    _lib.call("oscar_store_int2", kr.data_ptr(), vr.data_ptr(), n, history.data_ptr(), slots.data_ptr(),
+              counts.data_ptr(), geo, clip_params(cfg, "k"), clip_params(cfg, "v"), _stream(history))
+
+
+def rotate_store(key, value, rk, rv, history, slots, counts, layout, query=None, debug_rotated=False):
+    """Fused ``rotate(K,Rk)``, ``rotate(V,Rv)``, ``store_int2`` and optionally
+    ``rotate(Q,Rk)`` in one launch.  Returns ``qrot`` (or None) and, with
+    ``debug_rotated``, the bf16 rotated K/V rows that were quantised."""
+    _require_cuda(key, value, rk, rv, history, slots, counts, query)
+    cfg = layout.config
+    n = key.shape[0]
+    key, value = _rows(key), _rows(value)
+    rk, rv = rk.contiguous(), rv.contiguous()
+    qrot = kout = vout = None
+    qargs = (None, 0, 0, 0, None)
+    if query is not None:
+        query = _rows(query)
+        qrot = torch.empty(query.shape, device=query.device, dtype=torch.bfloat16)
+        qargs = (query.data_ptr(), query.stride(0), query.stride(1), query.shape[1], qrot.data_ptr())
+    if debug_rotated:
+        kout = torch.empty((n, layout.kv_heads, 256), device=key.device, dtype=torch.bfloat16)
+        vout = torch.empty_like(kout)
+    geo = geometry(layout, layout.kv_heads, 1)
+    _lib.call("oscar_rotate_store", key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(),
+              value.stride(0), value.stride(1), n, rk.data_ptr(), rv.data_ptr(), history.data_ptr(),
+              slots.data_ptr(), counts.data_ptr(), geo, clip_params(cfg, "k"), clip_params(cfg, "v"),
+              *qargs, _ptr(kout), _ptr(vout), _stream(key))
+    if debug_rotated:
+        return qrot, kout, vout
+    return qrot
+
+
+def prepare_tasks(qstarts, counts, tasks, task_count, max_reqs, query_tile, num_reqs=None, source_table=None,
+                  table=None, copy_columns=0):
+    """Compact (request, query offset) task table (reference kernels.py:262-287)."""
+    _require_cuda(qstarts, counts, tasks, task_count, source_table, table)
+    copy = source_table is not None and table is not None and copy_columns > 0
+    if copy and source_table.stride(1) != 1:
+        source_table = source_table.contiguous()
+    _lib.call("oscar_prepare_tasks", qstarts.data_ptr(), counts.data_ptr(), tasks.data_ptr(),
+              task_count.data_ptr(), tasks.shape[0], max_reqs, query_tile,
+              source_table.data_ptr() if copy else None, source_table.stride(0) if copy else 0,
+              table.data_ptr() if copy else None, table.stride(0) if copy else 0, copy_columns if copy else 0,
+              _stream(counts))
+
+
+def _meta_common(meta, layout, hq):
+    geo = geometry(layout, hq, meta.block_tables.stride(0))
+    if meta.block_tables.stride(1) != 1:
+        raise ValueError("block table rows must be contiguous")
+    # Launch only the query-row tiles this step can use: a task never holds more than
+    # min(queries_per_tile, max_query_len) queries (host scheduler value, no device read).
+    max_q = getattr(meta, "max_query_len", None)
+    if isinstance(max_q, int) and max_q > 0:
+        geo.query_tile = min(geo.query_tile, max_q)
+    return geo
+
+
+def attention_partials(query, key, value, history, window, meta, layout, scale, splits, raw):
+    """Split-KV attention partials (reference kernels.py:439-482)."""
+    _require_cuda(query, key, value, history, window)
+    n, hq, d = query.shape
+    partials = torch.empty((n, hq, splits, d), dtype=torch.float32, device=query.device)
+    lse = torch.empty((n, hq, splits), dtype=torch.float32, device=query.device)
+    if n == 0:
+        return partials, lse
+    query = _rows(query)
+    key, value = _rows(key), _rows(value)
+    geo = _meta_common(meta, layout, hq)
+    programs = attention_programs(n, meta.max_num_reqs, layout.config.queries_per_tile)
+    _lib.call("oscar_attention_partials", query.data_ptr(), query.stride(0), query.stride(1), key.data_ptr(),
+              key.stride(0), key.stride(1), value.data_ptr(), value.stride(0), value.stride(1),
+              history.data_ptr(), window.data_ptr(), meta.query_start_loc.data_ptr(), meta.seq_lens.data_ptr(),
+              meta.block_tables.data_ptr(), meta.counts.data_ptr(), meta.tasks.data_ptr(),
+              meta.task_count.data_ptr(), min(programs, meta.tasks.shape[0]), n, partials.data_ptr(),
+              lse.data_ptr(), geo, float(scale), int(splits), int(bool(raw)), _stream(query))
+    return partials, lse
+
+
+def merge_splits(partials, lse, counts):
+    """LSE merge of split partials (reference kernels.py:506-511)."""
+    _require_cuda(partials, lse, counts)
+    n, hq, splits, d = partials.shape
+    out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=partials.device)
+    logsum = torch.empty((n, hq), dtype=torch.float32, device=partials.device)
+    if n:
+        _lib.call("oscar_merge_splits", partials.contiguous().data_ptr(), lse.contiguous().data_ptr(), n, hq, splits,
+                  counts.data_ptr(), out.data_ptr(), logsum.data_ptr(), _stream(partials))
+    return out, logsum
+
+
+def merge_paths(history_out, history_lse, raw_partials, raw_lse, counts, output):
+    """LSE merge of the history and raw paths into ``output`` (reference kernels.py:530-541)."""
+    _require_cuda(history_out, history_lse, raw_partials, raw_lse, counts, output)
+    n, hq, d = history_out.shape
+    if n == 0:
+        return
+    if not output.is_contiguous():
+        raise ValueError("output must be contiguous")
+    a = history_out.contiguous()
+    b = raw_partials.contiguous()
+    lb = raw_lse.contiguous()
+    b_stride = b.shape[2] * d if b.ndim == 4 else d
+    lb_stride = lb.shape[2] if lb.ndim == 3 else 1
+    _lib.call("oscar_merge_paths", a.data_ptr(), history_lse.contiguous().data_ptr(), b.data_ptr(), b_stride,
+              lb.data_ptr(), lb_stride, n, hq, counts.data_ptr(), output.data_ptr(), _stream(a))
+
+
+def store_windows(key, value, window, meta, layout):
+    """Write current BF16 K/V into the sink/ring window (reference kernels.py:598-620)."""
+    _require_cuda(key, value, window)
+    key, value = _rows(key), _rows(value)
+    geo = _meta_common(meta, layout, layout.kv_heads)
+    programs = min(key.shape[0], meta.max_num_reqs)
+    _lib.call("oscar_store_windows", key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(),
+              value.stride(0), value.stride(1), window.data_ptr(), meta.query_start_loc.data_ptr(),
+              meta.seq_lens.data_ptr(), meta.block_tables.data_ptr(), meta.counts.data_ptr(), programs, geo,
+              _stream(key))
+
+
+def dequant_inverse_rotate(history, slots, rk, rv, layout):
+    """Diagnostic finite tile only (reference kernels.py:651-672)."""
+    _require_cuda(history, slots, rk, rv)
+    n, h = slots.numel(), layout.kv_heads
+    if n > 4096:
+        raise ValueError("diagnostic dequant is limited to 4096 tokens; use fused attention")
+    k = torch.empty((n, h, 256), device=history.device, dtype=torch.bfloat16)
+    v = torch.empty_like(k)
+    geo = geometry(layout, h, 1)
+    _lib.call("oscar_unpack", history.data_ptr(), slots.contiguous().data_ptr(), n, geo, k.data_ptr(),
+              v.data_ptr(), _stream(history))
+    return rotate(k, rk.T), rotate(v, rv.T)
+
+
+# ----------------------------------------------------------------------------
+# fused decode step
+# ----------------------------------------------------------------------------
+
+
+class DecodeScratch:
+    """Caller-owned split scratch: fp32 partials [n, Hq, splits+1, 256] and lse."""
+
+    def __init__(self, max_tokens: int, hq: int, splits: int, device):
+        self.splits = splits
+        self.partials = torch.empty((max_tokens, hq, splits + 1, 256), dtype=torch.float32, device=device)
+        self.lse = torch.empty((max_tokens, hq, splits + 1), dtype=torch.float32, device=device)
+
+
+def decode_attention(qrot, query, key, value, history, window, meta, layout, scale, splits, rv, output, scratch=None,
+                     store_window=True):
+    """History + raw attention, split merge, inverse V rotation, path merge and the
+    window store of one decode / MTP-verify step (reference backend.py:195-226)."""
+    _require_cuda(qrot, query, key, value, history, window, rv, output)
+    n, hq, _ = query.shape
+    if n == 0:
+        return output
+    if scratch is None or scratch.partials.shape[0] < n or scratch.splits != splits:
+        scratch = DecodeScratch(n, hq, splits, query.device)
+    query, key, value = _rows(query), _rows(key), _rows(value)
+    qrot = qrot.contiguous()
+    rv = rv.contiguous()
+    geo = _meta_common(meta, layout, hq)
+    programs = min(attention_programs(n, meta.max_num_reqs, layout.config.queries_per_tile), meta.tasks.shape[0])
+    window_programs = min(n, meta.max_num_reqs) if store_window else 0
+    _lib.call("oscar_decode_attention", qrot.data_ptr(), query.data_ptr(), query.stride(0), query.stride(1),
+              key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(), value.stride(0), value.stride(1),
+              history.data_ptr(), window.data_ptr(), meta.query_start_loc.data_ptr(), meta.seq_lens.data_ptr(),
+              meta.block_tables.data_ptr(), meta.counts.data_ptr(), meta.tasks.data_ptr(),
+              meta.task_count.data_ptr(), programs, n, rv.data_ptr(), scratch.partials.data_ptr(),
+              scratch.lse.data_ptr(), output.data_ptr(), geo, float(scale), int(splits), window_programs,
+              _stream(query))
+    return output
+
+
+def default_scale(head_dim: int = 256) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,36 @@
+"""The C-ABI library loads on a CPU host and exports every symbol the header declares."""
+
+import re
+from pathlib import Path
+
+from oscar_new_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "oscar_b200.h").read_text()
+    return sorted(set(re.findall(r"^int (oscar_\w+)\(", text, flags=re.M)))
+
+
+def test_header_and_binding_agree():
+    assert declared_symbols() == sorted(_lib.exported_symbols())
+
+
+def test_library_loads_and_exports_every_symbol():
+    handle = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(handle, name), name
+    assert handle.oscar_version() == 100
+
+
+def test_invalid_arguments_are_rejected_without_launch():
+    handle = _lib.lib()
+    geo = _lib.Geometry(kv_heads=4, group=6, head_dim=128, block_tokens=768, kernel_block=128, slot_bytes=160,
+                        vector_bytes=68, sink=4, recent=128, ring=129, table_stride=8, query_tile=4,
+                        page_bytes=768 * 4 * 256 * 2)
+    clip = _lib.Clip(enabled=0, mode=0, asc_lo=0, asc_hi=0, weight=0.0, factor=1.0)
+    # head_dim != 256 is refused before any device work
+    assert handle.oscar_store_int2(None, None, 4, None, None, None, geo, clip, clip, None) == 1
+    assert handle.oscar_jacobi_rotations(None, 1, 0, 1e-6, None, None, None, None) == 1
+    assert handle.oscar_rotate(None, 0, 1, 0, 0, 1, None, 0, 0, None, None) == 1
