@@ -1,0 +1,487 @@
+"""Benchmark of the OSCAR INT2 decode-attention layer on B200.
+
+Workload: one FULL attention layer, 24 query heads / 4 KV heads,
+D=256, batch 64 requests per GPU with 32768 context tokens each (4 BF16 sink tokens,
+128-token BF16 recent window, 1 current token, INT2 history for the rest), physical
+pages of 768 tokens handed out by a seeded random permutation, 16 KV splits with LSE
+merge.  A step is one layer forward of the drop-in path: task table, fused rotation +
+INT2 store of the current K/V (+ Q rotation), paged split-KV history attention, BF16
+sink/recent/current attention, split merge + inverse V rotation + path merge, window
+store.  Synthetic seeded data (no dataset offline); the cache is filled by the same
+store kernels.  Weak scaling: every rank owns its own 64 requests; ranks share nothing
+on the data path (torch.distributed is used only for the barrier and max-over-ranks
+timing).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from dataclasses import replace
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+B, H, G, D, SEQ, SINK, RECENT, SPLITS, BP = 64, 4, 6, 256, 32768, 4, 128, 16, 768
+METRIC = "int2_decode_attention_kv_tokens_per_s"
+UNIT = "KV tokens/s"
+HISTORY_BYTES_PER_TOKEN_HEAD = 136  # packed K + V vectors of one (token, KV head)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def workload_sizes():
+    hist_tokens = SEQ - 1 - SINK - RECENT  # prefix minus sink and recent
+    hist_bytes = B * H * hist_tokens * HISTORY_BYTES_PER_TOKEN_HEAD
+    window_bytes = B * H * (SINK + RECENT) * 2 * D * 2
+    current = B * (H * G + 2 * H) * D * 2
+    out = B * H * G * D * 2
+    return dict(
+        kv_tokens=B * SEQ * H,
+        history_bytes=hist_bytes,
+        footprint_bytes=B * H * hist_tokens * 160,
+        algorithmic_bytes=hist_bytes + window_bytes + current + out,
+    )
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+
+def build_state(device, seed):
+    from oscar_new_b200 import kernels
+    from oscar_new_b200.config import OscarConfig
+    from oscar_new_b200.layout import CacheLayout
+    from oscar_new_b200.synthetic import cache_stripes, plan_pages, rotation
+
+    cfg = replace(OscarConfig(), sink_tokens=SINK, recent_tokens=RECENT, speculative_tokens=0)
+    layout = CacheLayout(BP, kv_heads=H, config=cfg)
+    plan = plan_pages([SEQ] * B, [1] * B, BP, seed=seed)
+    cache = cache_stripes(plan.num_pages, BP, H, device)
+    history, window = layout.tensor_views(cache)
+    rk = rotation(1).bfloat16().to(device)
+    rv = rotation(2).bfloat16().to(device)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    prefix = SEQ - 1
+    # fill every request's prefix with the device store kernels (history + window)
+    for req in range(B):
+        k = torch.randn(prefix, H, D, device=device, generator=gen)
+        k[..., :8] *= 20
+        k = k.bfloat16()
+        v = torch.randn(prefix, H, D, device=device, generator=gen).bfloat16()
+        slots = plan.slots_of(req, range(prefix)).to(device)
+        counts = torch.tensor([1, prefix], dtype=torch.int32, device=device)
+        kernels.rotate_store(k, v, rk, rv, history, slots, counts, layout)
+        meta1 = plan.meta(device)
+        meta1.query_start_loc = torch.tensor([0, prefix], dtype=torch.int32, device=device)
+        meta1.seq_lens = torch.tensor([prefix], dtype=torch.int32, device=device)
+        meta1.block_tables = plan.block_tables[req : req + 1].to(device).contiguous()
+        meta1.counts = counts
+        meta1.max_num_reqs = 1
+        kernels.store_windows(k, v, window, meta1, layout)
+        del k, v
+    meta = plan.meta(device, cfg.queries_per_tile)
+    q = torch.randn(B, H * G, D, device=device, generator=gen).bfloat16()
+    k = torch.randn(B, H, D, device=device, generator=gen)
+    k[..., :8] *= 20
+    k = k.bfloat16()
+    v = torch.randn(B, H, D, device=device, generator=gen).bfloat16()
+    torch.cuda.synchronize(device)
+    return dict(cfg=cfg, layout=layout, plan=plan, cache=cache, history=history, window=window, rk=rk, rv=rv,
+                meta=meta, q=q, k=k, v=v)
+
+
+def layer_step(st, out, scratch):
+    """One drop-in layer forward (what OscarAttentionImpl.forward launches)."""
+    from oscar_new_b200 import kernels
+
+    m = st["meta"]
+    kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
+                          st["cfg"].queries_per_tile)
+    qrot = kernels.rotate_store(st["k"], st["v"], st["rk"], st["rv"], st["history"], m.slot_mapping, m.counts,
+                                st["layout"], query=st["q"])
+    kernels.decode_attention(qrot, st["q"], st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                             1.0 / math.sqrt(D), SPLITS, st["rv"], out, scratch)
+    return qrot
+
+
+LAUNCHES_PER_STEP = 6  # tasks, rotate+store, history, raw, finalize, window store
+
+
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def traffic_per_launch():
+    """dram bytes per history-kernel launch from the committed ncu summary (scaled)."""
+    p = ROOT / "profiles" / "history_attention_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d["dram_bytes_per_launch_scaled_to_bench"]
+
+
+def run_gpu(args):
+    from oscar_new_b200 import _lib, kernels
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    _lib.lib()
+    st = build_state(device, seed=1234 + rank)
+    sizes = workload_sizes()
+    out = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=device)
+    scratch = kernels.DecodeScratch(B, H * G, SPLITS, device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident step (value) ----
+    for _ in range(args.warmup):
+        layer_step(st, out, scratch)
+    barrier()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            layer_step(st, out, scratch)
+        e1.record(stream)
+        barrier()
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    if not bool(torch.isfinite(out.float()).all()):
+        raise RuntimeError("non-finite attention output")
+
+    # ---- dominant kernel alone: history split-KV attention, CUDA events on its stream ----
+    m = st["meta"]
+    qrot = kernels.rotate(st["q"], st["rk"])
+    for _ in range(3):
+        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                                   1.0 / math.sqrt(D), SPLITS, False)
+    barrier()
+    reps = max(5, args.steps)
+    e0.record(stream)
+    for _ in range(reps):
+        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                                   1.0 / math.sqrt(D), SPLITS, False)
+    e1.record(stream)
+    barrier()
+    kern_ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+
+    # ---- end to end through the public API with host buffers ----
+    pin = {name: st[name].cpu().pin_memory() for name in ("q", "k", "v")}
+    meta_host = {name: getattr(m, name).cpu().pin_memory() for name in ("query_start_loc", "seq_lens", "slot_mapping")}
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in list(pin.values()) + list(meta_host.values()))
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for name, t in pin.items():
+            st[name].copy_(t, non_blocking=True)
+        for name, t in meta_host.items():
+            getattr(m, name).copy_(t, non_blocking=True)
+        layer_step(st, out, scratch)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = sizes["history_bytes"] / (kern_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": world * sizes["kv_tokens"] / (step_ms * 1e-3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int2-kv/bf16",
+            "data": "synthetic (seeded N(0,1) bf16, K channels 0-7 x20, random-permutation pages)",
+            "config": {
+                "workload": "config3 single-query paged INT2 decode attention layer (store + attention + merge)",
+                "requests_per_gpu": B, "context": SEQ, "q_heads": H * G, "kv_heads": H, "head_dim": D,
+                "sink": SINK, "recent": RECENT, "kv_splits": SPLITS, "page_tokens": BP,
+                "l2": "inputs larger than L2 (packed history 1.14 GB per GPU)",
+                "us_per_layer": step_ms * 1e3,
+                "hbm_gbs_algorithmic": sizes["algorithmic_bytes"] / (step_ms * 1e-3) / 1e9,
+                "frac_of_8tbs_packed_history": sizes["history_bytes"] / (step_ms * 1e-3) / 8e12,
+                "parallelism": f"weak x{world}, shard = requests x KV heads, no data-path collective",
+            },
+            "roofline": {
+                "kernel": "history_attention_kernel",
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_kind": f"{peak_kind} hbm copy GB/s",
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "us_per_launch": kern_ms * 1e3,
+                "algorithmic_bytes_per_launch": sizes["history_bytes"],
+                "traffic": traffic_per_launch(),
+            },
+            "e2e": {
+                "value": world * sizes["kv_tokens"] / (e2e_ms * 1e-3),
+                "unit": UNIT,
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms,
+            },
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(st, budget_s=args.cpu_budget)
+        print(json.dumps(line), flush=True)
+    del scratch
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
+# CPU reference arm: the oracle port of the reference's algorithm on the host cores
+# ----------------------------------------------------------------------------
+
+
+def oracle_decode_sample(history, window, meta, layout, qrot, q, k, v, rv, requests):
+    """Decode step of `requests` through the CPU oracle (history in the rotated space,
+    raw BF16 path, merges, inverse rotation).  Inputs are host tensors."""
+    from types import SimpleNamespace
+
+    from oracle import int2_oracle as oo
+
+    outs = []
+    for req in requests:
+        sub = SimpleNamespace(
+            query_start_loc=torch.tensor([0, 1], dtype=torch.int32),
+            seq_lens=meta.seq_lens[req : req + 1].clone(),
+            block_tables=meta.block_tables[req : req + 1].clone(),
+            counts=torch.tensor([1, 1], dtype=torch.int32),
+        )
+        out, _, _ = oo.decode_reference(qrot[req : req + 1], q[req : req + 1], k[req : req + 1], v[req : req + 1],
+                                        history, window, sub, layout, 1.0 / math.sqrt(D), rv)
+        outs.append(out)
+    return torch.cat(outs)
+
+
+def cpu_baseline(st, budget_s=20.0):
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oscar_new_b200 import kernels
+
+    hist = st["history"].cpu().numpy()
+    win = st["window"].cpu()
+    meta = st["meta"]
+    mh = type("M", (), {})()
+    mh.seq_lens = meta.seq_lens.cpu()
+    mh.block_tables = meta.block_tables.cpu()
+    qrot = kernels.rotate(st["q"], st["rk"]).cpu()
+    q, k, v, rv = st["q"].cpu(), st["k"].cpu(), st["v"].cpu(), st["rv"].cpu()
+    done = 0
+    t0 = time.perf_counter()
+    out = None
+    while done < B and time.perf_counter() - t0 < budget_s:
+        out = oracle_decode_sample(hist, win, mh, st["layout"], qrot, q, k, v, rv, [done])
+        done += 1
+    dt = time.perf_counter() - t0
+    check = None
+    if out is not None:
+        # spot parity of the last sampled request against the GPU output
+        gpu = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=st["q"].device)
+        scratch = kernels.DecodeScratch(B, H * G, SPLITS, st["q"].device)
+        layer_step(st, gpu, scratch)
+        g = gpu.view(B, H * G, D)[done - 1].float().cpu()
+        check = float((g - out[0]).norm() / out[0].norm())
+    return {
+        "value": done * SEQ * H / dt,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"{done} of {B} config-3 requests through the CPU oracle decode step ({dt:.1f} s)",
+        "gpu_vs_oracle_rel_err": check,
+    }
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oracle import int2_oracle as oo
+    from oscar_new_b200.config import OscarConfig
+    from oscar_new_b200.layout import CacheLayout
+    from oscar_new_b200.synthetic import plan_pages, rotation
+
+    cfg = replace(OscarConfig(), sink_tokens=SINK, recent_tokens=RECENT, speculative_tokens=0)
+    layout = CacheLayout(BP, kv_heads=H, config=cfg)
+    # one request of the config, built with the oracle's own packer on the host
+    plan = plan_pages([SEQ], [1], BP, seed=7)
+    pages = plan.num_pages
+    hist = torch.full((pages * layout.stripe_page_bytes,), 0x5A, dtype=torch.uint8).numpy()
+    win = torch.zeros(pages * layout.stripe_page_bytes // 2, dtype=torch.bfloat16)
+    gen = torch.Generator().manual_seed(7)
+    rk, rv = rotation(1).bfloat16(), rotation(2).bfloat16()
+    prefix = SEQ - 1
+    chunk = 4096
+    for s0 in range(0, prefix, chunk):
+        n = min(chunk, prefix - s0)
+        kk = torch.randn(n, H, D, generator=gen)
+        kk[..., :8] *= 20
+        kr = (kk.bfloat16().float() @ rk.float()).bfloat16()
+        vr = (torch.randn(n, H, D, generator=gen).bfloat16().float() @ rv.float()).bfloat16()
+        packed = oo.packed_slots(kr, vr, cfg).numpy()
+        slots = plan.slots_of(0, range(s0, s0 + n)).numpy()
+        for h in range(H):
+            addr = oo.slot_addresses(slots, h, layout)
+            hist[addr[:, None] + torch.arange(136).numpy()[None, :]] = packed[:, h, :136]
+    q = torch.randn(1, H * G, D, generator=gen).bfloat16()
+    k = torch.randn(1, H, D, generator=gen).bfloat16()
+    v = torch.randn(1, H, D, generator=gen).bfloat16()
+    qrot = (q.float() @ rk.float()).bfloat16()
+    mh = type("M", (), {})()
+    mh.seq_lens = torch.tensor([SEQ], dtype=torch.int32)
+    mh.block_tables = plan.block_tables
+    for _ in range(args.warmup):
+        oracle_decode_sample(hist, win, mh, layout, qrot, q, k, v, rv, [0])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle_decode_sample(hist, win, mh, layout, qrot, q, k, v, rv, [0])
+    dt = (time.perf_counter() - t0) / args.steps
+    value = SEQ * H / dt
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int2-kv/fp32",
+        "data": "synthetic (seeded, same generators as the GPU arm)",
+        "config": {"workload": "config3 decode attention, one request per step (bounded CPU sample)",
+                   "context": SEQ, "q_heads": H * G, "kv_heads": H, "head_dim": D},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "1 config-3 request (32768 tokens x 4 KV heads) per step through the CPU oracle"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="oscar", choices=["oscar", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()
