@@ -7,7 +7,8 @@
  * synchronises the host, nothing reads device memory from the host, and nothing
  * allocates: every buffer is owned by the caller.  Entry points are safe to call
  * from several host threads on distinct streams and can be recorded in CUDA graphs
- * (all data-dependent bounds are read on the device from `counts`).
+ * (all data-dependent bounds are read on the device from `counts`); the
+ * no-allocation decode variant below carries its own notes instead.
  *
  * Tensor conventions (row-major unless strides are given):
  *   bf16/f16 are passed as raw 16-bit payloads (void*); D (head_dim) is 256.
@@ -159,6 +160,28 @@ int oscar_decode_attention(const void *qrot, const void *query, int64_t qs0, int
                            const void *rv, float *scratch_partials, float *scratch_lse,
                            void *output, oscar_geometry geo, float scale, int32_t splits,
                            int32_t window_programs, void *stream);
+
+/* oscar_decode_attention without caller scratch, for callers that cannot allocate
+ * device memory during decode (an engine whose memory plan already gave all free
+ * memory to the KV cache, or an FFI host with no device allocator).  No counterpart in
+ * the reference.  The split scratch is a fixed file-scope device array of
+ * oscar_decode_attention_noalloc_max_rows() rows (n * Hq * (splits + 1) <= 32768, i.e.
+ * 32 MiB of partials) held by every GPU that loads the library; larger calls return
+ * OSCAR_ERR_INVALID.  The first call on a device looks up the array's address (make it
+ * before any stream capture).  All calls on a device share the array, so calls whose GPU
+ * work overlaps race; sequential calls need no clearing.  Nothing is allocated. */
+int oscar_decode_attention_noalloc(const void *qrot, const void *query, int64_t qs0, int64_t qs1,
+                                   const void *key, int64_t ks0, int64_t ks1, const void *value,
+                                   int64_t vs0, int64_t vs1, const uint8_t *history, void *window,
+                                   const int32_t *qstarts, const int32_t *seq_lens,
+                                   const int32_t *table, const int32_t *counts,
+                                   const int32_t *tasks, const int32_t *task_count,
+                                   int32_t num_tasks, int64_t n, const void *rv, void *output,
+                                   oscar_geometry geo, float scale, int32_t splits,
+                                   int32_t window_programs, void *stream);
+
+/* Row capacity of the built-in scratch of oscar_decode_attention_noalloc. */
+int64_t oscar_decode_attention_noalloc_max_rows(void);
 
 /* ---- calibration (reference oscar_ascend/calibration_kernels.py) -------------- */
 

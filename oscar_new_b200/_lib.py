@@ -65,7 +65,10 @@ _SIGNATURES = {
     "oscar_sst_weights": [P, I64, I32, I64, I64, P, P, P, P],
     "oscar_normalize": [P, I64, P, F32, P, P],
     "oscar_jacobi_rotations": [P, I32, I32, F32, P, P, P, P],
+    "oscar_decode_attention_noalloc": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P],
+    "oscar_decode_attention_noalloc_max_rows": [],
 }
+_RESTYPES = {"oscar_decode_attention_noalloc_max_rows": C.c_int64}
 
 
 def lib():
@@ -80,7 +83,7 @@ def lib():
         for name, args in _SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = args
-            fn.restype = C.c_int
+            fn.restype = _RESTYPES.get(name, C.c_int)
         _lib = handle
     return _lib
 

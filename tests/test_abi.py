@@ -10,7 +10,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def declared_symbols():
     text = (ROOT / "include" / "oscar_b200.h").read_text()
-    return sorted(set(re.findall(r"^int (oscar_\w+)\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:int|int64_t) (oscar_\w+)\(", text, flags=re.M)))
 
 
 def test_header_and_binding_agree():
