@@ -466,6 +466,32 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def set_requests(n):
+    global B
+    B = int(n)
+
+
+def profile_only(what):
+    """Small, self-ending workload for ncu captures (no timing, no JSON)."""
+    from oscar_new_b200 import kernels
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    st = build_state(device, seed=1234)
+    m = st["meta"]
+    out = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=device)
+    scratch = kernels.DecodeScratch(B, H * G, SPLITS, device)
+    qrot = kernels.rotate(st["q"], st["rk"])
+    for _ in range(4):
+        if what == "history":
+            kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                                       1.0 / math.sqrt(D), SPLITS, False)
+        else:
+            layer_step(st, out, scratch)
+    torch.cuda.synchronize(device)
+    print("profile run done", B, "requests", what)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -474,9 +500,16 @@ def main():
     ap.add_argument("--impl", default="oscar", choices=["oscar", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
+    ap.add_argument("--profile-kernel", choices=["history", "step"], default=None,
+                    help="build the state, run 4 launches of the history kernel (or 4 layer steps) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    set_requests(args.requests)
+    if args.profile_kernel:
+        profile_only(args.profile_kernel)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

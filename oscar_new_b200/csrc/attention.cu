@@ -81,8 +81,9 @@ OSCAR_DEVINL TaskInfo load_task(int task, const int32_t *tasks, const int32_t *t
 // are read in (lane t owns dims [64t, 64t+64)):
 //  * qf[js]: fp16 fragments of the exact code functional sum_d q_d c_d, k-step js = 4i+p
 //    covering dims 16(4t+i) + {p, 8+p | 4+p, 12+p}, pre-divided by 4^p;
-//  * qb[j]:  int8 fragments (per-row scale) of the bit functionals, k32-step j = 2i+h
-//    covering dims 16(4t+i) + 4b + 2h (+1 for the second register), b = 0..3;
+//  * qb[j]:  int8 fragments (per-row scale) of the bit functionals, k32-step j = 2p+pr
+//    covering position p of words 4t + 2pr (first register) and 4t + 2pr + 1 (second),
+//    i.e. dims 16(4t+2pr) + 4b + p and 16(4t+2pr+1) + 4b + p, b = 0..3;
 //  * qsum / qscale of the rows 2t, 2t+1 this lane accumulates.
 struct QueryFrags {
   uint32_t qf[16][2];
@@ -125,17 +126,17 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
   const float inv = amax > 0.f ? 127.0f / amax : 0.f;
   auto q8 = [&](int d) { return (uint32_t)(min(max(__float2int_rn(dim(d) * inv), -127), 127) & 0xff); };
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int p = 0; p < 4; ++p)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int pr = 0; pr < 2; ++pr) {
       uint32_t r0 = 0, r1 = 0;
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        r0 |= q8(16 * i + 4 * b + 2 * h) << (8 * b);
-        r1 |= q8(16 * i + 4 * b + 2 * h + 1) << (8 * b);
+        r0 |= q8(16 * (2 * pr) + 4 * b + p) << (8 * b);
+        r1 |= q8(16 * (2 * pr + 1) + 4 * b + p) << (8 * b);
       }
-      Q.qb[2 * i + h][0] = r0;
-      Q.qb[2 * i + h][1] = r1;
+      Q.qb[2 * p + pr][0] = r0;
+      Q.qb[2 * p + pr][1] = r1;
     }
   // s / scale are row-gi values on all four t lanes; the S fragment needs rows 2t, 2t+1.
   Q.qsum[0] = __shfl_sync(0xffffffffu, s, 8 * t);
@@ -146,7 +147,10 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
 
 // Per-token coefficients of q.k with k = bf16(c*s + z) (the reference rounds the
 // dequantised key to bf16):  q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
-// with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.
+// with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.  Since
+// sum(q c) = sum(q b0) + 2 sum(q b1), the kernel uses M = sum(q c) (exact fp16 MMA) and
+// the two low-precision int8 sums A = sum(q b0), C = sum(q b0 b1):
+//   q.k = v0*sum(q) + (d1 + a/2) M - (a/2) A + b C.
 struct KeyCoef {
   float v0, d1, a, b;
 };
@@ -165,7 +169,7 @@ OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
   return k;
 }
 
-template <int MAXW>
+template <int MAXW, int NM>
 __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(HistParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   const oscar_geometry &g = P.geo;
@@ -246,7 +250,6 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f}, zp_run[2] = {0.f, 0.f};
   const float sl2 = P.scale_log2;
-  const int mtiles = CT / 16;
   bool ok = true;
 
 #pragma unroll 1
@@ -259,67 +262,113 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
     }
     const uint8_t *stage = stages + s * P.stage_bytes;
     const int cpos = (first_chunk + c) * CT;
-#pragma unroll 1
-    for (int mt = sub; mt < mtiles; mt += P.warps_per_unit) {
-      const int tpos = cpos + 16 * mt;
-      if (tpos + 16 <= lo || tpos >= hi) continue;  // warp-uniform
-      const uint8_t *tile = stage + (16 * mt) * token_bytes + head_local * g.slot_bytes;
-      // ---- S^T (tokens x rows): exact sum q c on fp16, bit functionals on int8 ----
-      const uint4 ka = *reinterpret_cast<const uint4 *>(tile + gi * token_bytes + 16 * t);
-      const uint4 kb = *reinterpret_cast<const uint4 *>(tile + (gi + 8) * token_bytes + 16 * t);
-      const uint32_t kaw[4] = {ka.x, ka.y, ka.z, ka.w}, kbw[4] = {kb.x, kb.y, kb.z, kb.w};
-      float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
-      int cb[4] = {0, 0, 0, 0}, cc[4] = {0, 0, 0, 0};
+    // this warp's NM consecutive 16-token m-tiles of the chunk
+    const int mt0 = sub * NM;
+    if (cpos + 16 * (mt0 + NM) > lo && cpos + 16 * mt0 < hi) {  // warp-uniform
+      const uint8_t *tl[NM];
+      bool va[NM], vb[NM];
+#pragma unroll
+      for (int j = 0; j < NM; ++j) {
+        const int tpos = cpos + 16 * (mt0 + j);
+        tl[j] = stage + (16 * (mt0 + j)) * token_bytes + head_local * g.slot_bytes;
+        va[j] = tpos + gi >= lo && tpos + gi < hi;
+        vb[j] = tpos + gi + 8 >= lo && tpos + gi + 8 < hi;
+      }
+      // ---- S^T (tokens x rows): exact sum q c on fp16, bit sums on int8 ----
+      uint32_t kaw[NM][4], kbw[NM][4];
+#pragma unroll
+      for (int j = 0; j < NM; ++j) {
+        const uint4 ka = *reinterpret_cast<const uint4 *>(tl[j] + gi * token_bytes + 16 * t);
+        const uint4 kb = *reinterpret_cast<const uint4 *>(tl[j] + (gi + 8) * token_bytes + 16 * t);
+        kaw[j][0] = ka.x, kaw[j][1] = ka.y, kaw[j][2] = ka.z, kaw[j][3] = ka.w;
+        kbw[j][0] = kb.x, kbw[j][1] = kb.y, kbw[j][2] = kb.z, kbw[j][3] = kb.w;
+      }
+      float sc[NM][4], sd[NM][4];
+#pragma unroll
+      for (int j = 0; j < NM; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[j][e] = sd[j][e] = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint32_t a_sh = kaw[i] >> 8, b_sh = kbw[i] >> 8;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
           const uint32_t msk = 0x00030003u << (2 * p);
-          mma_f16_16816((p & 1) ? sd : sc, kaw[i] & msk, kbw[i] & msk, a_sh & msk, b_sh & msk, Q.qf[4 * i + p][0],
-                        Q.qf[4 * i + p][1]);
-        }
-        const uint32_t a1 = kaw[i] >> 1, b1 = kbw[i] >> 1;  // bit 0 of each pair -> high bits b1
-        const uint32_t ay = kaw[i] & a1, by = kbw[i] & b1;  // b0 & b1 at the even bits
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int p0 = 2 * h, p1 = 2 * h + 1;
-          mma_s8_16832(cb, (a1 >> (2 * p0)) & 0x01010101u, (b1 >> (2 * p0)) & 0x01010101u,
-                       (a1 >> (2 * p1)) & 0x01010101u, (b1 >> (2 * p1)) & 0x01010101u, Q.qb[2 * i + h][0],
-                       Q.qb[2 * i + h][1]);
-          mma_s8_16832(cc, (ay >> (2 * p0)) & 0x01010101u, (by >> (2 * p0)) & 0x01010101u,
-                       (ay >> (2 * p1)) & 0x01010101u, (by >> (2 * p1)) & 0x01010101u, Q.qb[2 * i + h][0],
-                       Q.qb[2 * i + h][1]);
+          for (int j = 0; j < NM; ++j) {
+            mma_f16_16816((p & 1) ? sd[j] : sc[j], kaw[j][i] & msk, kbw[j][i] & msk, (kaw[j][i] >> 8) & msk,
+                          (kbw[j][i] >> 8) & msk, Q.qf[4 * i + p][0], Q.qf[4 * i + p][1]);
+          }
         }
       }
+      // A = sum q b0 and C = sum q b0 b1.  Operands are single masks of the packed word
+      // (u8 values 4^p); positions are accumulated from p = 3 down with an exact >> 2
+      // between groups, which leaves sum_p (.)_p at unit weight.
+      uint32_t kay[NM][4], kby[NM][4];
+      int acc_a[NM][4], acc_c[NM][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sc[e] += sd[e];
+      for (int j = 0; j < NM; ++j) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          kay[j][i] = kaw[j][i] & (kaw[j][i] >> 1);
+          kby[j][i] = kbw[j][i] & (kbw[j][i] >> 1);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc_a[j][e] = acc_c[j][e] = 0;
+      }
+#pragma unroll
+      for (int p = 3; p >= 0; --p) {
+        if (p < 3) {
+#pragma unroll
+          for (int j = 0; j < NM; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc_a[j][e] >>= 2, acc_c[j][e] >>= 2;
+        }
+        const uint32_t m = 0x01010101u << (2 * p);
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const int w0 = 2 * pr, w1 = 2 * pr + 1;
+#pragma unroll
+          for (int j = 0; j < NM; ++j) {
+            mma_u8s8_16832(acc_a[j], kaw[j][w0] & m, kbw[j][w0] & m, kaw[j][w1] & m, kbw[j][w1] & m,
+                           Q.qb[2 * p + pr][0], Q.qb[2 * p + pr][1]);
+            mma_u8s8_16832(acc_c[j], kay[j][w0] & m, kby[j][w0] & m, kay[j][w1] & m, kby[j][w1] & m,
+                           Q.qb[2 * p + pr][0], Q.qb[2 * p + pr][1]);
+          }
+        }
+      }
       // ---- logits (log2 domain) ----
-      const uint32_t kszA = *reinterpret_cast<const uint32_t *>(tile + gi * token_bytes + 64);
-      const uint32_t kszB = *reinterpret_cast<const uint32_t *>(tile + (gi + 8) * token_bytes + 64);
-      const uint32_t vszA = *reinterpret_cast<const uint32_t *>(tile + gi * token_bytes + g.vector_bytes + 64);
-      const uint32_t vszB = *reinterpret_cast<const uint32_t *>(tile + (gi + 8) * token_bytes + g.vector_bytes + 64);
-      const bool va = tpos + gi >= lo && tpos + gi < hi;
-      const bool vb = tpos + gi + 8 >= lo && tpos + gi + 8 < hi;
-      const KeyCoef ca = key_coefficients(kszA), cbk = key_coefficients(kszB);
-      float lg[4];
+      float lg[NM][4];
+      uint32_t vsz[NM][2];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const KeyCoef &kc = e < 2 ? ca : cbk;
-        const int r = e & 1;
-        float dot = kc.v0 * Q.qsum[r];
-        dot = fmaf(kc.d1 * kTwo24, sc[e], dot);
-        dot = fmaf(kc.a * Q.qscale[r], (float)cb[e], dot);
-        dot = fmaf(kc.b * Q.qscale[r], (float)cc[e], dot);
-        lg[e] = ((e < 2) ? va : vb) ? dot * sl2 : -INFINITY;
+      for (int j = 0; j < NM; ++j) {
+        const uint32_t kszA = *reinterpret_cast<const uint32_t *>(tl[j] + gi * token_bytes + 64);
+        const uint32_t kszB = *reinterpret_cast<const uint32_t *>(tl[j] + (gi + 8) * token_bytes + 64);
+        vsz[j][0] = *reinterpret_cast<const uint32_t *>(tl[j] + gi * token_bytes + g.vector_bytes + 64);
+        vsz[j][1] = *reinterpret_cast<const uint32_t *>(tl[j] + (gi + 8) * token_bytes + g.vector_bytes + 64);
+        const KeyCoef ka = key_coefficients(kszA), kb = key_coefficients(kszB);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const KeyCoef &kc = e < 2 ? ka : kb;
+          const int r = e & 1;
+          const float ha = 0.5f * kc.a;
+          float dot = kc.v0 * Q.qsum[r];
+          dot = fmaf((kc.d1 + ha) * kTwo24, sc[j][e] + sd[j][e], dot);
+          dot = fmaf(-ha * Q.qscale[r], (float)acc_a[j][e], dot);
+          dot = fmaf(kc.b * Q.qscale[r], (float)acc_c[j][e], dot);
+          lg[j][e] = ((e < 2) ? va[j] : vb[j]) ? dot * sl2 : -INFINITY;
+        }
       }
-      // ---- online softmax with lazy re-basing ----
-      float mx[2] = {fmaxf(lg[0], lg[2]), fmaxf(lg[1], lg[3])};
+      // ---- online softmax over the warp's 16*NM tokens, lazy re-basing ----
+      float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 4));
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 8));
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 16));
+      for (int j = 0; j < NM; ++j) {
+        mx[0] = fmaxf(mx[0], fmaxf(lg[j][0], lg[j][2]));
+        mx[1] = fmaxf(mx[1], fmaxf(lg[j][1], lg[j][3]));
+      }
+#pragma unroll
+      for (int o2 = 4; o2 <= 16; o2 <<= 1) {
+        mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o2));
+        mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o2));
       }
       const bool need0 = mx[0] > m_run[0] + kRescaleSlack || (m_run[0] == -INFINITY && mx[0] > -INFINITY);
       const bool need1 = mx[1] > m_run[1] + kRescaleSlack || (m_run[1] == -INFINITY && mx[1] > -INFINITY);
@@ -336,39 +385,50 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
       }
       const float ms0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
       const float ms1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
-      const float p0 = ex2(lg[0] - ms0), p1 = ex2(lg[1] - ms1), p2 = ex2(lg[2] - ms0), p3 = ex2(lg[3] - ms1);
-      const float vsA = va ? half_bits_to_float(vszA & 0xffffu) : 0.f;
-      const float vzA = va ? half_bits_to_float(vszA >> 16) : 0.f;
-      const float vsB = vb ? half_bits_to_float(vszB & 0xffffu) : 0.f;
-      const float vzB = vb ? half_bits_to_float(vszB >> 16) : 0.f;
-      l_run[0] += p0 + p2;
-      l_run[1] += p1 + p3;
-      zp_run[0] = fmaf(p0, vzA, fmaf(p2, vzB, zp_run[0]));
-      zp_run[1] = fmaf(p1, vzA, fmaf(p3, vzB, zp_run[1]));
-      // P'^T fragments: (token, row) -> transposed to (row, token)
-      const uint32_t pb0 = movmatrix_trans(pack_half2(p0 * vsA, p1 * vsA));
-      const uint32_t pb1 = movmatrix_trans(pack_half2(p2 * vsB, p3 * vsB));
-      // ---- O^T += Vc^T . P'^T (dims x rows) ----
-      const uint8_t *vt = tile + g.vector_bytes;
-      uint32_t vw[4][2];  // [token 2t,2t+1,2t+8,2t+9][word 2gi, 2gi+1]
+      uint32_t pb[NM][2];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int tok = 2 * t + (q & 1) + (q >> 1) * 8;
-        const uint32_t *src = reinterpret_cast<const uint32_t *>(vt + tok * token_bytes) + 2 * gi;
-        vw[q][0] = src[0];
-        vw[q][1] = src[1];
+      for (int j = 0; j < NM; ++j) {
+        const float p0 = ex2(lg[j][0] - ms0), p1 = ex2(lg[j][1] - ms1);
+        const float p2 = ex2(lg[j][2] - ms0), p3 = ex2(lg[j][3] - ms1);
+        const float vsA = va[j] ? half_bits_to_float(vsz[j][0] & 0xffffu) : 0.f;
+        const float vzA = va[j] ? half_bits_to_float(vsz[j][0] >> 16) : 0.f;
+        const float vsB = vb[j] ? half_bits_to_float(vsz[j][1] & 0xffffu) : 0.f;
+        const float vzB = vb[j] ? half_bits_to_float(vsz[j][1] >> 16) : 0.f;
+        l_run[0] += p0 + p2;
+        l_run[1] += p1 + p3;
+        zp_run[0] = fmaf(p0, vzA, fmaf(p2, vzB, zp_run[0]));
+        zp_run[1] = fmaf(p1, vzA, fmaf(p3, vzB, zp_run[1]));
+        // P'^T fragments: (token, row) -> transposed to (row, token)
+        pb[j][0] = movmatrix_trans(pack_half2(p0 * vsA, p1 * vsA));
+        pb[j][1] = movmatrix_trans(pack_half2(p2 * vsB, p3 * vsB));
       }
+      // ---- O^T += Vc^T . P'^T (dims x rows) ----
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t sel = (uint32_t)b | ((uint32_t)(4 + b) << 8);
-        const uint32_t x0 = prmt(vw[0][0], vw[1][0], sel);  // word 2gi, tokens 2t,2t+1
-        const uint32_t x1 = prmt(vw[0][1], vw[1][1], sel);  // word 2gi+1
-        const uint32_t x2 = prmt(vw[2][0], vw[3][0], sel);  // word 2gi, tokens 2t+8,2t+9
-        const uint32_t x3 = prmt(vw[2][1], vw[3][1], sel);
+      for (int j = 0; j < NM; ++j) {
+        const uint8_t *vt = tl[j] + g.vector_bytes;
+        uint32_t vw[4][2];  // [token 2t,2t+1,2t+8,2t+9][word 2gi, 2gi+1]
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const uint32_t msk = 0x00030003u << (2 * p);
-          mma_f16_16816(o[4 * b + p], x0 & msk, x1 & msk, x2 & msk, x3 & msk, pb0, pb1);
+        for (int q = 0; q < 4; ++q) {
+          const int tok = 2 * t + (q & 1) + (q >> 1) * 8;
+          const uint32_t *src = reinterpret_cast<const uint32_t *>(vt + tok * token_bytes) + 2 * gi;
+          vw[q][0] = src[0];
+          vw[q][1] = src[1];
+        }
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          // bytes (2hb, 2hb+1) of token a in the low half, of token b in the high half
+          const uint32_t sel = hb ? 0x7632u : 0x5410u;
+          const uint32_t x0 = prmt(vw[0][0], vw[1][0], sel);  // word 2gi, tokens 2t,2t+1
+          const uint32_t x1 = prmt(vw[0][1], vw[1][1], sel);  // word 2gi+1
+          const uint32_t x2 = prmt(vw[2][0], vw[3][0], sel);  // word 2gi, tokens 2t+8,2t+9
+          const uint32_t x3 = prmt(vw[2][1], vw[3][1], sel);
+          const uint32_t y0 = x0 >> 8, y1 = x1 >> 8, y2 = x2 >> 8, y3 = x3 >> 8;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const uint32_t msk = 0x00030003u << (2 * p);
+            mma_f16_16816(o[4 * (2 * hb) + p], x0 & msk, x1 & msk, x2 & msk, x3 & msk, pb[j][0], pb[j][1]);
+            mma_f16_16816(o[4 * (2 * hb + 1) + p], y0 & msk, y1 & msk, y2 & msk, y3 & msk, pb[j][0], pb[j][1]);
+          }
         }
       }
     }
@@ -769,17 +829,23 @@ struct FinalParams {
   __nv_bfloat16 *out;
 };
 
-__global__ void __launch_bounds__(kGemmThreads) finalize_kernel(FinalParams P) {
+// 16-row tiles, 4 warps: one CTA per 16 output rows, so a decode step (n * Hq rows)
+// spreads over n * Hq / 16 CTAs.
+constexpr int kFinRows = 16;
+constexpr int kFinThreads = 128;
+constexpr int kFinSmem = (kFinRows * kDim + 2 * kBStageElems) * 2 + 2 * kFinRows * 4;
+
+__global__ void __launch_bounds__(kFinThreads) finalize_kernel(FinalParams P) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
-  __nv_bfloat16 *sB = sA + kAElems;
-  float *s_la = reinterpret_cast<float *>(sB + 2 * kBStageElems);  // [64]
-  float *s_lb = s_la + kTileRows;
+  __nv_bfloat16 *sB = sA + kFinRows * kDim;
+  float *s_la = reinterpret_cast<float *>(sB + 2 * kBStageElems);  // [16]
+  float *s_lb = s_la + kFinRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t row0 = (int64_t)blockIdx.x * kTileRows;
+  const int64_t row0 = (int64_t)blockIdx.x * kFinRows;
   const int32_t active = P.counts[1];
-  for (int i = 0; i < kTileRows / 8; ++i) {
-    const int r = warp * 8 + i;
+  for (int i = 0; i < kFinRows / 4; ++i) {
+    const int r = warp * (kFinRows / 4) + i;
     const int64_t row = row0 + r;
     const bool valid = row < P.rows && row / P.hq < active;
     float m = -INFINITY;
@@ -811,37 +877,35 @@ __global__ void __launch_bounds__(kGemmThreads) finalize_kernel(FinalParams P) {
       s_lb[r] = valid ? P.lse[row * P.split_slots + P.splits] : -INFINITY;
     }
   }
-  float acc[2][8][4];
-  rowgemm_mainloop(acc, sA, sB, BMatrix{P.rv, 1, 256});  // B(k, n) = Rv[n][k]
-  const int wm = warp >> 2, wn = warp & 3, gq = lane >> 2, t = lane & 3;
+  float acc[1][8][4];
+  rowgemm_mainloop<1, kFinThreads>(acc, sA, sB, BMatrix{P.rv, 1, 256});  // B(k, n) = Rv[n][k]
+  const int wn = warp & 3, gq = lane >> 2, t = lane & 3;
 #pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
+  for (int hb = 0; hb < 2; ++hb) {
+    const int r = gq + 8 * hb;
+    const int64_t row = row0 + r;
+    if (row >= P.rows) continue;
+    const float xa = s_la[r], xb = s_lb[r];
+    float m = fmaxf(xa, xb);
+    m = m == -INFINITY ? 0.f : m;
+    const float wa = expf(xa - m), wb = expf(xb - m);
+    const float inv = 1.0f / fmaxf(wa + wb, 1e-30f);
+    const float *braw = P.partials + (row * P.split_slots + P.splits) * kDim;
 #pragma unroll
-    for (int hb = 0; hb < 2; ++hb) {
-      const int r = wm * 32 + mi * 16 + gq + 8 * hb;
-      const int64_t row = row0 + r;
-      if (row >= P.rows) continue;
-      const float xa = s_la[r], xb = s_lb[r];
-      float m = fmaxf(xa, xb);
-      m = m == -INFINITY ? 0.f : m;
-      const float wa = expf(xa - m), wb = expf(xb - m);
-      const float inv = 1.0f / fmaxf(wa + wb, 1e-30f);
-      const float *braw = P.partials + (row * P.split_slots + P.splits) * kDim;
-#pragma unroll
-      for (int nj = 0; nj < 8; ++nj) {
-        const int col = wn * 64 + nj * 8 + 2 * t;
-        // hout is rounded to bf16 (the reference rotate writes bf16)
-        const float h0 = bf16_bits_to_float(float_to_bf16_bits(acc[mi][nj][2 * hb]));
-        const float h1 = bf16_bits_to_float(float_to_bf16_bits(acc[mi][nj][2 * hb + 1]));
-        float b0 = 0.f, b1 = 0.f;
-        if (wb != 0.f) {
-          const float2 bb = *reinterpret_cast<const float2 *>(braw + col);
-          b0 = bb.x, b1 = bb.y;
-        }
-        const float r0 = (wa * h0 + wb * b0) * inv, r1 = (wa * h1 + wb * b1) * inv;
-        *reinterpret_cast<uint32_t *>(P.out + row * kDim + col) = pack_bf162(r0, r1);
+    for (int nj = 0; nj < 8; ++nj) {
+      const int col = wn * 64 + nj * 8 + 2 * t;
+      // hout is rounded to bf16 (the reference rotate writes bf16)
+      const float h0 = round_bf16(acc[0][nj][2 * hb]);
+      const float h1 = round_bf16(acc[0][nj][2 * hb + 1]);
+      float b0 = 0.f, b1 = 0.f;
+      if (wb != 0.f) {
+        const float2 bb = *reinterpret_cast<const float2 *>(braw + col);
+        b0 = bb.x, b1 = bb.y;
       }
+      const float r0 = (wa * h0 + wb * b0) * inv, r1 = (wa * h1 + wb * b1) * inv;
+      *reinterpret_cast<uint32_t *>(P.out + row * kDim + col) = pack_bf162(r0, r1);
     }
+  }
 }
 
 // ----------------------------------------------------------------------------
@@ -867,20 +931,15 @@ __global__ void __launch_bounds__(256) window_store_kernel(const __nv_bfloat16 *
   const int prefix = seq - (qend - qstart);
   if (qend <= qstart) return;
   const int64_t owner = (int64_t)table[(int64_t)req * g.table_stride] / (g.block_tokens / kKernelBlock);
-  const int entries = (g.sink + g.ring) * g.kv_heads;
+  // Positions this step writes: sink positions in [prefix, min(seq, S)) and, for the
+  // ring, each slot's latest writer, i.e. pos >= S with pos + C >= seq.  Same set as
+  // the reference's per-slot latest-writer rule (kernels.py:576-582).
+  const int lo = max(prefix, 0);
+  const int entries = (seq - lo) * g.kv_heads;
   for (int e = warp; e < entries; e += 8) {
-    const int idx = e / g.kv_heads, head = e % g.kv_heads;
-    int pos;
-    if (idx < g.sink) {
-      pos = idx;
-    } else {
-      const int residue = idx - g.sink;
-      int mod = (seq - 1 - residue) % g.ring;
-      if (mod < 0) mod += g.ring;
-      pos = seq - 1 - mod;
-    }
-    const bool valid = pos >= prefix && pos < seq && (idx < g.sink || pos >= g.sink);
-    if (!valid) continue;
+    const int pos = lo + e / g.kv_heads, head = e % g.kv_heads;
+    if (!(pos < g.sink || pos + g.ring >= seq)) continue;
+    const int idx = pos < g.sink ? pos : g.sink + pos % g.ring;
     const int cur = qstart + pos - prefix;
     const uint4 kv0 = *reinterpret_cast<const uint4 *>(key + (int64_t)cur * ks0 + (int64_t)head * ks1 + lane * 8);
     const uint4 kv1 = *reinterpret_cast<const uint4 *>(value + (int64_t)cur * vs0 + (int64_t)head * vs1 + lane * 8);
@@ -965,20 +1024,23 @@ static bool geo_ok(const oscar_geometry &g) {
          g.recent >= 0 && g.query_tile > 0 && g.table_stride > 0;
 }
 
-template <int MAXW>
+template <int MAXW, int NM>
 static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStream_t stream) {
   static size_t configured = 0;
   if (smem > configured) {
-    if (cudaFuncSetAttribute(history_attention_kernel<MAXW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(history_attention_kernel<MAXW, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return OSCAR_ERR_LAUNCH;
     configured = smem;
   }
-  history_attention_kernel<MAXW><<<grid, 32 * (P.consumers + 1), smem, stream>>>(P);
+  history_attention_kernel<MAXW, NM><<<grid, 32 * (P.consumers + 1), smem, stream>>>(P);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
 }
 
+// Launch shape: each consumer warp owns one (KV head, 8-row) unit and NM = 2
+// consecutive 16-token m-tiles of every chunk; a chunk is all heads of
+// 16 * NM * warps_per_unit tokens (at most one 128-token kernel block).
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) {
   const oscar_geometry &g = P.geo;
   const int rows = g.query_tile * g.group;
@@ -989,19 +1051,21 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) 
   if (g.kv_heads % hpc) hpc = 1;
   P.heads_per_cta = hpc;
   P.units = hpc * P.ntiles;
-  P.warps_per_unit = P.units >= 8 ? 1 : 8 / P.units;
-  P.consumers = P.units * P.warps_per_unit;
-  int ct = 128;
-  while (ct > 16 && ct * hpc * g.slot_bytes > 20480) ct >>= 1;
-  P.chunk_tokens = ct;
-  P.stage_bytes = ct * hpc * g.slot_bytes;
+  constexpr int NM = 2;
+  int wpu = P.units >= 8 ? 1 : 8 / P.units;
+  while (wpu > 1 && 16 * NM * wpu > kKernelBlock) wpu >>= 1;
+  P.warps_per_unit = wpu;
+  P.consumers = P.units * wpu;
+  P.chunk_tokens = 16 * NM * wpu;
+  P.stage_bytes = P.chunk_tokens * hpc * g.slot_bytes;
   const size_t xch = ((size_t)(P.consumers - P.units) * (16 * 4 * 32 + 2 * 32) + (size_t)P.consumers * 4 * 32) * 4;
   size_t smem = 128 + (size_t)kStages * P.stage_bytes;
   if (smem < 128 + xch) smem = 128 + xch;
+  if (smem > 227 * 1024) return OSCAR_ERR_UNSUPPORTED;
   dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
-  if (P.consumers <= 8) return launch_history<8>(P, grid, smem, stream);
-  if (P.consumers <= 12) return launch_history<12>(P, grid, smem, stream);
-  return launch_history<16>(P, grid, smem, stream);
+  if (P.consumers <= 8) return launch_history<8, NM>(P, grid, smem, stream);
+  if (P.consumers <= 12) return launch_history<12, NM>(P, grid, smem, stream);
+  return launch_history<16, NM>(P, grid, smem, stream);
 }
 
 static int raw_launch(const RawParams &P, int32_t num_tasks, cudaStream_t stream) {
@@ -1178,9 +1242,8 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     if (rc) return rc;
   }
   static bool configured = false;
-  const int fsmem = kRowGemmSmem + 2 * kTileRows * 4;
   if (!configured) {
-    if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fsmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFinSmem) != cudaSuccess)
       return OSCAR_ERR_LAUNCH;
     configured = true;
   }
@@ -1189,7 +1252,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
   F.rows = n * hq, F.hq = hq, F.counts = counts;
   F.rv = reinterpret_cast<const __nv_bfloat16 *>(rv);
   F.out = reinterpret_cast<__nv_bfloat16 *>(output);
-  finalize_kernel<<<(unsigned)((F.rows + kTileRows - 1) / kTileRows), kGemmThreads, fsmem, st>>>(F);
+  finalize_kernel<<<(unsigned)((F.rows + kFinRows - 1) / kFinRows), kFinThreads, kFinSmem, st>>>(F);
   OSCAR_CHECK_LAUNCH();
   if (window_programs > 0) {
     window_store_kernel<<<window_programs, 256, 0, st>>>(

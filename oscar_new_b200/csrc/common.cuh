@@ -93,6 +93,15 @@ OSCAR_DEVINL void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+OSCAR_DEVINL void mma_u8s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                 uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Transpose an 8x8 b16 matrix held one 32-bit pair per lane (row = lane/4).
 OSCAR_DEVINL uint32_t movmatrix_trans(uint32_t x) {
   uint32_t r;

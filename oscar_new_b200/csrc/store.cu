@@ -64,10 +64,14 @@ struct RotateParams {
   oscar_clip clip[2];
 };
 
-__global__ void __launch_bounds__(kGemmThreads) rotate_kernel(RotateParams p) {
+template <int ROWS>
+__global__ void __launch_bounds__(ROWS == 64 ? 256 : 128) rotate_kernel(RotateParams p) {
+  constexpr int MI = ROWS == 64 ? 2 : 1;
+  constexpr int NT = ROWS == 64 ? 256 : 128;
+  constexpr int NW = NT / 32;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __nv_bfloat16 *sA = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
-  __nv_bfloat16 *sB = sA + kAElems;
+  __nv_bfloat16 *sB = sA + ROWS * kDim;
   int64_t tile = blockIdx.x;
   int j = 0;
   while (j < p.njobs - 1 && tile >= p.job[j].tiles) {
@@ -76,20 +80,19 @@ __global__ void __launch_bounds__(kGemmThreads) rotate_kernel(RotateParams p) {
   }
   const RotateJob job = p.job[j];
   const int64_t nrows = job.n * job.h;
-  const int64_t row0 = tile * kTileRows;
-  load_a_tile(sA, row0, nrows, [&](int64_t r) {
+  const int64_t row0 = tile * ROWS;
+  load_a_tile<ROWS, NT>(sA, row0, nrows, [&](int64_t r) {
     return job.x + (r / job.h) * job.s0 + (r % job.h) * job.s1;
   });
   cp_async_commit();
-  float acc[2][8][4];
-  rowgemm_mainloop(acc, sA, sB, job.r);
+  float acc[MI][8][4];
+  rowgemm_mainloop<MI, NT>(acc, sA, sB, job.r);
   // acc -> bf16 tile (rounded exactly once, as the reference rotate output)
-  store_acc_bf16(sA, acc);
+  store_acc_bf16<MI>(sA, acc);
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (job.kv < 0 || job.y != nullptr) {
-    // copy the bf16 tile out: 64 rows x 32 chunks
-    for (int c = threadIdx.x; c < kTileRows * 32; c += kGemmThreads) {
+    for (int c = threadIdx.x; c < ROWS * 32; c += NT) {
       const int r = c >> 5, ch = c & 31;
       if (row0 + r < nrows)
         *reinterpret_cast<uint4 *>(job.y + (row0 + r) * kDim + ch * 8) =
@@ -99,8 +102,8 @@ __global__ void __launch_bounds__(kGemmThreads) rotate_kernel(RotateParams p) {
   if (job.kv < 0) return;
   const int32_t active = p.counts[1];
 #pragma unroll 1
-  for (int i = 0; i < kTileRows / 8; ++i) {
-    const int r = warp * (kTileRows / 8) + i;
+  for (int i = 0; i < ROWS / NW; ++i) {
+    const int r = warp * (ROWS / NW) + i;
     const int64_t row = row0 + r;
     if (row >= nrows) break;  // warp-uniform
     const int64_t token = row / job.h;
@@ -118,6 +121,39 @@ __global__ void __launch_bounds__(kGemmThreads) rotate_kernel(RotateParams p) {
     uint8_t *dst = p.history + slot_byte_offset(slot, head, p.geo) + job.kv * p.geo.vector_bytes;
     quantize_pack_warp(x, p.clip[job.kv], dst, true);
   }
+}
+
+// Launch with 64-row tiles for large row counts, 16-row tiles (4x the CTAs) when the
+// 64-row grid would not fill two waves of the GPU (decode-sized steps).
+static int launch_rotate(RotateParams p, cudaStream_t stream) {
+  int64_t rows64 = 0;
+  for (int j = 0; j < p.njobs; ++j) rows64 += (p.job[j].n * p.job[j].h + 63) / 64;
+  const bool small = rows64 < 2 * 148;
+  const int rows = small ? 16 : 64;
+  int64_t total = 0;
+  for (int j = 0; j < p.njobs; ++j) {
+    p.job[j].tiles = (p.job[j].n * p.job[j].h + rows - 1) / rows;
+    total += p.job[j].tiles;
+  }
+  const int smem = (rows * kDim + 2 * kBStageElems) * 2;
+  static bool configured[2] = {false, false};
+  if (small) {
+    if (!configured[0]) {
+      if (cudaFuncSetAttribute(rotate_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return OSCAR_ERR_LAUNCH;
+      configured[0] = true;
+    }
+    rotate_kernel<16><<<(unsigned)total, 128, smem, stream>>>(p);
+  } else {
+    if (!configured[1]) {
+      if (cudaFuncSetAttribute(rotate_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return OSCAR_ERR_LAUNCH;
+      configured[1] = true;
+    }
+    rotate_kernel<64><<<(unsigned)total, 256, smem, stream>>>(p);
+  }
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
 }
 
 // ----------------------------------------------------------------------------
@@ -175,17 +211,6 @@ static bool clip_ok(const oscar_clip &c) {
          c.weight >= 0.f && c.weight < 1.f;
 }
 
-static int set_smem_once() {
-  static bool done = false;
-  if (!done) {
-    if (cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowGemmSmem) !=
-        cudaSuccess)
-      return OSCAR_ERR_LAUNCH;
-    done = true;
-  }
-  return OSCAR_OK;
-}
-
 }  // namespace oscar
 
 using namespace oscar;
@@ -197,15 +222,12 @@ extern "C" int oscar_rotate(const void *x, int64_t n, int32_t h, int64_t xs0, in
   if (n < 0 || h <= 0 || xs2 != 1 || !y) return OSCAR_ERR_INVALID;
   if (n == 0) return OSCAR_OK;
   if (!rows_ok(x, xs0, xs1) || !rotation_ok(r, rs0, rs1)) return OSCAR_ERR_INVALID;
-  if (set_smem_once() != OSCAR_OK) return OSCAR_ERR_LAUNCH;
   RotateParams p{};
   p.njobs = 1;
   p.job[0] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(x), xs0, xs1, n, h,
                        BMatrix{reinterpret_cast<const __nv_bfloat16 *>(r), rs0, rs1},
-                       reinterpret_cast<__nv_bfloat16 *>(y), -1, (n * h + kTileRows - 1) / kTileRows};
-  rotate_kernel<<<(unsigned)p.job[0].tiles, kGemmThreads, kRowGemmSmem, (cudaStream_t)stream>>>(p);
-  OSCAR_CHECK_LAUNCH();
-  return OSCAR_OK;
+                       reinterpret_cast<__nv_bfloat16 *>(y), -1, 0};
+  return launch_rotate(p, (cudaStream_t)stream);
 }
 
 extern "C" int oscar_store_int2(const void *krot, const void *vrot, int64_t n, void *history,
@@ -235,8 +257,7 @@ extern "C" int oscar_rotate_store(const void *key, int64_t ks0, int64_t ks1, con
   if (!rows_ok(key, ks0, ks1) || !rows_ok(value, vs0, vs1)) return OSCAR_ERR_INVALID;
   if (!rotation_ok(rk, 256, 1) || !rotation_ok(rv, 256, 1)) return OSCAR_ERR_INVALID;
   if (query && (!rows_ok(query, qs0, qs1) || hq <= 0 || !qrot_out)) return OSCAR_ERR_INVALID;
-  if (set_smem_once() != OSCAR_OK) return OSCAR_ERR_LAUNCH;
-  const int64_t tiles = (n * geo.kv_heads + kTileRows - 1) / kTileRows;
+  const int64_t tiles = 0;  // set by launch_rotate
   RotateParams p{};
   p.history = reinterpret_cast<uint8_t *>(history);
   p.slots = slots;
@@ -251,18 +272,13 @@ extern "C" int oscar_rotate_store(const void *key, int64_t ks0, int64_t ks1, con
                        BMatrix{reinterpret_cast<const __nv_bfloat16 *>(rv), 256, 1},
                        reinterpret_cast<__nv_bfloat16 *>(vrot_out), 1, tiles};
   p.njobs = 2;
-  int64_t total = 2 * tiles;
   if (query) {
-    const int64_t qt = (n * hq + kTileRows - 1) / kTileRows;
     p.job[2] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(query), qs0, qs1, n, hq,
                          BMatrix{reinterpret_cast<const __nv_bfloat16 *>(rk), 256, 1},
-                         reinterpret_cast<__nv_bfloat16 *>(qrot_out), -1, qt};
+                         reinterpret_cast<__nv_bfloat16 *>(qrot_out), -1, 0};
     p.njobs = 3;
-    total += qt;
   }
-  rotate_kernel<<<(unsigned)total, kGemmThreads, kRowGemmSmem, (cudaStream_t)stream>>>(p);
-  OSCAR_CHECK_LAUNCH();
-  return OSCAR_OK;
+  return launch_rotate(p, (cudaStream_t)stream);
 }
 
 extern "C" int oscar_unpack(const uint8_t *history, const int64_t *slots, int64_t n, oscar_geometry geo,
