@@ -481,6 +481,8 @@ def profile_only(what):
     m = st["meta"]
     out = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=device)
     scratch = kernels.DecodeScratch(B, H * G, SPLITS, device)
+    kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
+                          st["cfg"].queries_per_tile)
     qrot = kernels.rotate(st["q"], st["rk"])
     for _ in range(4):
         if what == "history":
