@@ -466,6 +466,119 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------
+# secondary workloads (configs 2, 4, 5): their own JSON lines, not the headline
+# ----------------------------------------------------------------------------
+
+
+def _flush_l2(buf):
+    buf.add_(1)  # 256 MiB write: evicts the 126 MB L2 between timed iterations
+
+
+def _timed_each(fn, steps, warmup, device, flush):
+    """Sum of per-iteration CUDA-event durations on the launching stream, with an L2
+    flush (outside the timed interval) before every iteration."""
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in events:
+        _flush_l2(flush)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    return sum(e0.elapsed_time(e1) for e0, e1 in events) / steps
+
+
+def config2_state(device, seed=202):
+    """Config 2: 16384 tokens x 4 heads, K channels 0-7 x20, distinct seeded slots in 22
+    pages with every 64th slot -1, counts = [1, 16384], K/V clip .96/.92."""
+    from oscar_new_b200.config import OscarConfig
+    from oscar_new_b200.layout import CacheLayout
+    from oscar_new_b200.synthetic import cache_stripes, rotation
+
+    cfg = OscarConfig()
+    n, pages = 16384, 22
+    layout = CacheLayout(BP, kv_heads=H, config=cfg)
+    gen = torch.Generator().manual_seed(seed)
+    k = torch.randn(n, H, D, generator=gen)
+    k[..., :8] *= 20
+    v = torch.randn(n, H, D, generator=gen)
+    slots = torch.randperm(pages * BP, generator=gen)[:n].long()
+    slots[::64] = -1
+    cache = cache_stripes(pages, BP, H, device)
+    history, _ = layout.tensor_views(cache)
+    return dict(cfg=cfg, layout=layout, n=n, pages=pages, k=k.bfloat16().to(device), v=v.bfloat16().to(device),
+                rk=rotation(1).bfloat16().to(device), rv=rotation(2).bfloat16().to(device), slots=slots.to(device),
+                counts=torch.tensor([1, n], dtype=torch.int32, device=device), history=history)
+
+
+def run_rotate_store(args):
+    from oscar_new_b200 import _lib, kernels
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    _lib.lib()
+    st = config2_state(device)
+    n = st["n"]
+    flush = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=device)
+
+    def step():
+        kernels.rotate_store(st["k"], st["v"], st["rk"], st["rv"], st["history"], st["slots"], st["counts"],
+                             st["layout"])
+
+    with ClockSampler(0) as clocks:
+        ms = _timed_each(step, args.steps, args.warmup, device, flush)
+    live = int((st["slots"] >= 0).sum())
+    read_bytes = 2 * n * H * D * 2 + n * 8 + 2 * D * D * 2
+    write_bytes = 2 * live * H * 68
+    alg = read_bytes + write_bytes
+    flops = 2 * (2 * n * H * D * D)
+    peak, peak_kind = measured_peaks()
+    tflops_peak = _measured_tflops()
+    # end to end: pinned host K/V/slots in, the packed K stripe of the 22 pages out
+    pin = {name: st[name].cpu().pin_memory() for name in ("k", "v", "slots")}
+    hist_host = torch.empty(st["history"].shape, dtype=torch.uint8).pin_memory()
+
+    def e2e():
+        for name, t in pin.items():
+            st[name].copy_(t, non_blocking=True)
+        step()
+        hist_host.copy_(st["history"], non_blocking=True)
+
+    e2e_ms = _timed_each(e2e, args.steps, args.warmup, device, flush)
+    h2d = sum(t.numel() * t.element_size() for t in pin.values())
+    achieved = alg / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "int2_rotate_store_token_heads_per_s", "value": n * H / (ms * 1e-3), "unit": "token-heads/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16->int2", "data": "synthetic (seeded, config 2)",
+        "config": {"workload": "config2 fused K/V rotation + clip + INT2 pack/scatter (tcgen05 + TMA tiles)",
+                   "tokens": n, "kv_heads": H, "head_dim": D, "pages": st["pages"], "page_tokens": BP,
+                   "l2": "flushed (256 MiB write) before every timed iteration",
+                   "tensor_tflops": flops / (ms * 1e-3) / 1e12,
+                   "tensor_frac_of_measured_bf16": (flops / (ms * 1e-3) / 1e12) / tflops_peak},
+        "roofline": {"kernel": "rotate_tc_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm copy GB/s", "unit": "GB/s", "frac": achieved / peak,
+                     "us_per_launch": ms * 1e3, "algorithmic_bytes_per_launch": alg, "traffic": None},
+        "e2e": {"value": n * H / (e2e_ms * 1e-3), "unit": "token-heads/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": hist_host.numel(), "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _measured_tflops(kind="bf16_tflops"):
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if kind in d:
+            return float(d[kind])
+    return 1590.0
+
+
 def set_requests(n):
     global B
     B = int(n)
@@ -477,6 +590,14 @@ def profile_only(what):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
+    if what == "rotate-store":
+        cs = config2_state(device)
+        for _ in range(4):
+            kernels.rotate_store(cs["k"], cs["v"], cs["rk"], cs["rv"], cs["history"], cs["slots"], cs["counts"],
+                                 cs["layout"])
+        torch.cuda.synchronize(device)
+        print("profile run done: config 2 rotate-store")
+        return
     st = build_state(device, seed=1234)
     m = st["meta"]
     out = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=device)
@@ -503,8 +624,10 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
-    ap.add_argument("--profile-kernel", choices=["history", "step"], default=None,
-                    help="build the state, run 4 launches of the history kernel (or 4 layer steps) and exit")
+    ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store"], default=None,
+                    help="build the state, run 4 launches of the kernel (or 4 layer steps) and exit")
+    ap.add_argument("--workload", choices=["decode", "rotate-store"], default="decode",
+                    help="decode: config 3 (the headline); rotate-store: config 2")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -514,6 +637,8 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "rotate-store":
+        run_rotate_store(args)
     else:
         run_gpu(args)
 

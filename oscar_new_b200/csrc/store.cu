@@ -2,8 +2,7 @@
 //
 // Reference: oscar_ascend/kernels.py:14-66 (rotate), :69-202 (clip, store_int2),
 // :623-672 (unpack / dequant_inverse_rotate).
-#include "quant.cuh"
-#include "rowgemm.cuh"
+#include "rotate.cuh"
 
 namespace oscar {
 
@@ -40,30 +39,6 @@ __global__ void __launch_bounds__(256) store_int2_kernel(const __nv_bfloat16 *__
   }
 }
 
-// ----------------------------------------------------------------------------
-// rotation GEMM (+ optional fused quantise/store epilogue)
-// ----------------------------------------------------------------------------
-struct RotateJob {
-  const __nv_bfloat16 *x;  // rows (t, h) at x + t*s0 + h*s1, unit inner stride
-  int64_t s0, s1;
-  int64_t n;               // tokens
-  int32_t h;               // heads per token
-  BMatrix r;
-  __nv_bfloat16 *y;        // contiguous [n*h, 256] output (nullable for store jobs)
-  int32_t kv;              // -1: plain rotate, 0: K store, 1: V store
-  int64_t tiles;
-};
-
-struct RotateParams {
-  RotateJob job[3];
-  int32_t njobs;
-  uint8_t *history;
-  const int64_t *slots;
-  const int32_t *counts;
-  oscar_geometry geo;
-  oscar_clip clip[2];
-};
-
 template <int ROWS>
 __global__ void __launch_bounds__(ROWS == 64 ? 256 : 128) rotate_kernel(RotateParams p) {
   constexpr int MI = ROWS == 64 ? 2 : 1;
@@ -90,45 +65,20 @@ __global__ void __launch_bounds__(ROWS == 64 ? 256 : 128) rotate_kernel(RotatePa
   // acc -> bf16 tile (rounded exactly once, as the reference rotate output)
   store_acc_bf16<MI>(sA, acc);
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (job.kv < 0 || job.y != nullptr) {
-    for (int c = threadIdx.x; c < ROWS * 32; c += NT) {
-      const int r = c >> 5, ch = c & 31;
-      if (row0 + r < nrows)
-        *reinterpret_cast<uint4 *>(job.y + (row0 + r) * kDim + ch * 8) =
-            *reinterpret_cast<const uint4 *>(sA + r * kDim + ((ch ^ (r & 7)) << 3));
-    }
-  }
-  if (job.kv < 0) return;
-  const int32_t active = p.counts[1];
-#pragma unroll 1
-  for (int i = 0; i < ROWS / NW; ++i) {
-    const int r = warp * (ROWS / NW) + i;
-    const int64_t row = row0 + r;
-    if (row >= nrows) break;  // warp-uniform
-    const int64_t token = row / job.h;
-    const int head = (int)(row % job.h);
-    const int64_t slot = token < active ? p.slots[token] : -1;
-    if (slot < 0) continue;  // warp-uniform
-    const uint4 raw = *reinterpret_cast<const uint4 *>(sA + r * kDim + (((lane) ^ (r & 7)) << 3));
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    float x[8];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      x[2 * q] = bf16_bits_to_float(w[q] & 0xffffu);
-      x[2 * q + 1] = bf16_bits_to_float(w[q] >> 16);
-    }
-    uint8_t *dst = p.history + slot_byte_offset(slot, head, p.geo) + job.kv * p.geo.vector_bytes;
-    quantize_pack_warp(x, p.clip[job.kv], dst, true);
-  }
+  rotate_epilogue(sA, ROWS, row0, job, p, NW);
 }
 
-// Launch with 64-row tiles for large row counts, 16-row tiles (4x the CTAs) when the
-// 64-row grid would not fill two waves of the GPU (decode-sized steps).
+// Large row counts go to the tcgen05 kernel; 16-row tiles (4x the CTAs of 64-row ones)
+// serve launches whose 64-row grid would not fill two waves of the GPU (decode steps).
 static int launch_rotate(RotateParams p, cudaStream_t stream) {
   int64_t rows64 = 0;
   for (int j = 0; j < p.njobs; ++j) rows64 += (p.job[j].n * p.job[j].h + 63) / 64;
   const bool small = rows64 < 2 * 148;
+  if (!small) {
+    // tcgen05 + TMA tiles; geometries the TMA unit cannot describe use 64-row tiles
+    const int rc = launch_rotate_tc(p, stream);
+    if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
+  }
   const int rows = small ? 16 : 64;
   int64_t total = 0;
   for (int j = 0; j < p.njobs; ++j) {

@@ -127,6 +127,89 @@ def test_rotate_store_fused_bytes_and_rotation(cuda_lib):
             assert (got[off + 136 : off + 160] == 0x5A).all()
 
 
+def _check_store_bytes(history, layout, slots, krot, vrot, cfg):
+    """Every written slot bit-exact vs the oracle quantiser on the kernel's own bf16
+    rotated rows; every other byte of the stripe still holds the 0x5A sentinel."""
+    expect = oo.packed_slots(krot.cpu(), vrot.cpu(), cfg).numpy()  # [n, H, 160]
+    got = history.cpu().numpy()
+    written = np.zeros(got.shape[0], dtype=bool)
+    s = slots.cpu().numpy()
+    live = np.nonzero(s >= 0)[0]
+    for hh in range(layout.kv_heads):
+        addr = oo.slot_addresses(s[live], hh, layout)
+        idx = addr[:, None] + np.arange(136)[None, :]
+        np.testing.assert_array_equal(got[idx], expect[live, hh, :136])
+        written[idx.reshape(-1)] = True
+    assert (got[~written] == 0x5A).all()
+
+
+def test_rotate_store_config2_tcgen05(cuda_lib):
+    """Config 2 at full size: 16384 tokens x 4 heads (tcgen05 + TMA tiles), K/V clip
+    .96/.92, a seeded shuffle of distinct slots in 22 pages with every 64th slot -1."""
+    cfg = OscarConfig()
+    h, n, pages = 4, 16384, 22
+    layout = CacheLayout(768, kv_heads=h, config=cfg)
+    gen = torch.Generator().manual_seed(202)
+    k = torch.randn(n, h, 256, generator=gen)
+    k[..., :8] *= 20
+    k = k.bfloat16().to(DEV)
+    v = torch.randn(n, h, 256, generator=gen).bfloat16().to(DEV)
+    rk, rv = rotation(1).bfloat16().to(DEV), rotation(2).bfloat16().to(DEV)
+    slots = torch.randperm(pages * 768, generator=gen)[:n].long()
+    slots[::64] = -1
+    cache = cache_stripes(pages, 768, h, DEV)
+    history, _ = layout.tensor_views(cache)
+    counts = torch.tensor([1, n], dtype=torch.int32, device=DEV)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        _, krot, vrot = kernels.rotate_store(k, v, rk, rv, history, slots.to(DEV), counts, layout,
+                                             debug_rotated=True)
+        torch.cuda.synchronize()
+    names = {e.name for e in prof.events()}
+    assert any("rotate_tc_kernel" in nm for nm in names), names  # the tcgen05 path ran
+    torch.testing.assert_close(krot.float(), (k.float() @ rk.float()).bfloat16().float(), atol=0.03125, rtol=0.015)
+    torch.testing.assert_close(vrot.float(), (v.float() @ rv.float()).bfloat16().float(), atol=0.03125, rtol=0.015)
+    assert rel_err(krot, k.float() @ rk.float()) < 1e-2
+    _check_store_bytes(history, layout, slots, krot, vrot, cfg)
+
+
+def test_rotate_store_prefill_chunk_with_query_tcgen05(cuda_lib):
+    """K, V and Q jobs in one tcgen05 launch (Q: 24 heads -> 120-row tiles), strided
+    fused-QKV views, a token count that is not a tile multiple, counts below n."""
+    cfg = OscarConfig()
+    h, hq, n = 4, 24, 1031
+    layout = CacheLayout(768, kv_heads=h, config=cfg)
+    gen = torch.Generator().manual_seed(203)
+    qkv = torch.randn(n, hq + 2 * h, 256, generator=gen)
+    qkv[:, hq : hq + h, :8] *= 20
+    qkv = qkv.bfloat16().to(DEV)
+    q, k, v = qkv[:, :hq], qkv[:, hq : hq + h], qkv[:, hq + h :]
+    rk, rv = rotation(3).bfloat16().to(DEV), rotation(4).bfloat16().to(DEV)
+    slots = torch.randperm(2 * 768, generator=gen)[:n].long() + 768
+    cache = cache_stripes(3, 768, h, DEV)
+    history, _ = layout.tensor_views(cache)
+    active = n - 5
+    counts = torch.tensor([1, active], dtype=torch.int32, device=DEV)
+    qrot, krot, vrot = kernels.rotate_store(k, v, rk, rv, history, slots.to(DEV), counts, layout, query=q,
+                                            debug_rotated=True)
+    for got, x, r in ((qrot, q, rk), (krot, k, rk), (vrot, v, rv)):
+        torch.testing.assert_close(got.float().view(n, -1, 256), (x.float() @ r.float()).bfloat16().float(),
+                                   atol=0.03125, rtol=0.015)
+    masked = slots.clone()
+    masked[active:] = -1  # tokens at or beyond counts[1] are not stored
+    _check_store_bytes(history, layout, masked, krot.view(n, h, 256), vrot.view(n, h, 256), cfg)
+
+
+def test_rotate_large_column_major_rotation_tcgen05(cuda_lib):
+    """Plain rotation with a transposed (column-major) rotation view: the K-major B
+    operand path of the tcgen05 kernel; 6 heads per token (126-row tiles)."""
+    torch.manual_seed(8)
+    x = torch.randn(4096, 12, 256, device=DEV, dtype=torch.bfloat16)[:, ::2]
+    r = torch.linalg.qr(torch.randn(256, 256))[0].bfloat16().to(DEV).T
+    out = kernels.rotate(x, r)
+    ref = (x.float() @ r.float()).bfloat16().float()
+    torch.testing.assert_close(out.float(), ref, atol=0.03125, rtol=0.015)
+
+
 def test_unpack_matches_golden(cuda_lib):
     fx = load("unpack.pt")
     layout = CacheLayout(768, kv_heads=1)
