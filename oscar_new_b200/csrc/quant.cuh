@@ -124,6 +124,14 @@ OSCAR_DEVINL uint32_t half_umax(uint32_t v) {
   return v;
 }
 
+// Number of the 16 keys >= t, as four independent partial sums (short dependency chains).
+OSCAR_DEVINL uint32_t count_ge16(const uint32_t (&key)[16], uint32_t t) {
+  uint32_t c[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) c[i & 3] += key[i] >= t ? 1u : 0u;
+  return (c[0] + c[1]) + (c[2] + c[3]);
+}
+
 // k-th largest (1-indexed) 15-bit key of each half's 256 keys.  A key is a bf16
 // magnitude: exponent in bits 7-14, mantissa in bits 0-6.  The binade of the answer is
 // found first by counting keys >= e << 7 for e = the half's largest exponent and below
@@ -131,19 +139,16 @@ OSCAR_DEVINL uint32_t half_umax(uint32_t v) {
 // has not found its binade after 4 probes falls back to a 15-bit bisection.  Both
 // halves run the same number of counting steps (their counts share each reduction).
 OSCAR_DEVINL uint32_t half_kth_largest(const uint32_t (&key)[16], int k) {
-  uint32_t m = 0;
+  uint32_t m4[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) m = max(m, key[i]);
-  const int e = (int)(half_umax(m) >> 7);
+  for (int i = 0; i < 16; ++i) m4[i & 3] = max(m4[i & 3], key[i]);
+  const int e = (int)(half_umax(max(max(m4[0], m4[1]), max(m4[2], m4[3]))) >> 7);
   bool found = false;
   uint32_t v = 0;
 #pragma unroll 1
   for (int p = 0; p < 4; ++p) {
     const uint32_t t = (uint32_t)max(e - p, 0) << 7;
-    uint32_t c = 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) c += key[i] >= t ? 1u : 0u;
-    c = half_sum(c);
+    const uint32_t c = half_sum(count_ge16(key, t));
     if (!found && c >= (uint32_t)k) {
       found = true;
       v = t;
@@ -156,10 +161,7 @@ OSCAR_DEVINL uint32_t half_kth_largest(const uint32_t (&key)[16], int k) {
   for (int s = 0; s < steps; ++s) {
     const int b = nb - 1 - s;
     const uint32_t t = b >= 0 ? (v | (1u << b)) : 0xffffffffu;  // no key reaches 0xffffffff
-    uint32_t c = 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) c += key[i] >= t ? 1u : 0u;
-    if (half_sum(c) >= (uint32_t)k && b >= 0) v = t;
+    if (half_sum(count_ge16(key, t)) >= (uint32_t)k && b >= 0) v = t;
   }
   return v;
 }
@@ -184,14 +186,12 @@ OSCAR_DEVINL void quantize_pack_half(float (&x)[16], const oscar_clip &clip, uin
       const uint32_t hi_key = half_kth_largest(key, k_hi);
       uint32_t lo_key = hi_key;
       if (clip.asc_lo != clip.asc_hi) {
-        uint32_t ge = 0, below = 0;
+        uint32_t b4[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          ge += key[i] >= hi_key ? 1u : 0u;
-          if (key[i] < hi_key) below = max(below, key[i]);
-        }
-        ge = half_sum(ge);
-        below = half_umax(below);
+        for (int i = 0; i < 16; ++i)
+          if (key[i] < hi_key) b4[i & 3] = max(b4[i & 3], key[i]);
+        const uint32_t ge = half_sum(count_ge16(key, hi_key));
+        const uint32_t below = half_umax(max(max(b4[0], b4[1]), max(b4[2], b4[3])));
         if (ge < (uint32_t)(k_hi + 1)) lo_key = below;
       }
       const float a = __uint_as_float(lo_key << 16);
@@ -202,14 +202,14 @@ OSCAR_DEVINL void quantize_pack_half(float (&x)[16], const oscar_clip &clip, uin
 #pragma unroll
     for (int i = 0; i < 16; ++i) x[i] = fminf(fmaxf(x[i], -thr), thr);
   }
-  float lo = x[0], hi = x[0];
+  float lo4[4] = {x[0], x[1], x[2], x[3]}, hi4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-  for (int i = 1; i < 16; ++i) {
-    lo = fminf(lo, x[i]);
-    hi = fmaxf(hi, x[i]);
+  for (int i = 4; i < 16; ++i) {
+    lo4[i & 3] = fminf(lo4[i & 3], x[i]);
+    hi4[i & 3] = fmaxf(hi4[i & 3], x[i]);
   }
-  lo = half_min(lo);
-  hi = half_max(hi);
+  float lo = half_min(fminf(fminf(lo4[0], lo4[1]), fminf(lo4[2], lo4[3])));
+  float hi = half_max(fmaxf(fmaxf(hi4[0], hi4[1]), fmaxf(hi4[2], hi4[3])));
   const uint16_t zero_h = float_to_half_bits(lo);
   const uint16_t scale_h = float_to_half_bits(fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 3.0f), 6.103515625e-05f));
   const float zf = half_bits_to_float(zero_h);
@@ -219,7 +219,7 @@ OSCAR_DEVINL void quantize_pack_half(float (&x)[16], const oscar_clip &clip, uin
   // whenever q lies more than 1e-5 from an integer; otherwise (and for q < 0) the
   // IEEE division is done.
   const float inv = __frcp_rn(sf);
-  uint32_t packed = 0;
+  uint32_t pk[4] = {0, 0, 0, 0};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const float d = __fsub_rn(x[i], zf);
@@ -227,8 +227,9 @@ OSCAR_DEVINL void quantize_pack_half(float (&x)[16], const oscar_clip &clip, uin
     if (fabsf(__fsub_rn(__fsub_rn(q, truncf(q)), 0.5f)) > 0.49999f) q = __fadd_rn(__fdiv_rn(d, sf), 0.5f);
     int c = (int)q;  // truncation toward zero (torch .to(int32))
     c = min(max(c, 0), 3);
-    packed |= (uint32_t)c << (2 * i);
+    pk[i & 3] |= (uint32_t)c << (2 * i);
   }
+  const uint32_t packed = (pk[0] | pk[1]) | (pk[2] | pk[3]);
   if (write) {
     reinterpret_cast<uint32_t *>(dst)[l] = packed;
     if (l == 0) *reinterpret_cast<uint32_t *>(dst + kDataBytes) = (uint32_t)scale_h | ((uint32_t)zero_h << 16);

@@ -38,8 +38,9 @@ struct RotateParams {
 // Epilogue over a staged tile of `rows` rotated rows (swizzled like the A tile, see
 // a_index) starting at global row `row0` (valid while row < nrows): copy to y, then
 // quantise + scatter K / V rows, two rows per warp.  `nw` warps of the CTA take part.
+// `tile_slots` (optional, shared memory) holds the slot of each token of the tile.
 OSCAR_DEVINL void rotate_epilogue(const __nv_bfloat16 *sY, int rows, int64_t row0, const RotateJob &job,
-                                  const RotateParams &p, int nw) {
+                                  const RotateParams &p, int nw, const int64_t *tile_slots = nullptr) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nt = nw * 32;
   const int64_t nrows = job.n * job.h;
@@ -66,7 +67,10 @@ OSCAR_DEVINL void rotate_epilogue(const __nv_bfloat16 *sY, int rows, int64_t row
     if (live) {
       const int64_t token = row / job.h;
       head = (int)(row % job.h);
-      slot = token < active ? p.slots[token] : -1;
+      if (tile_slots != nullptr)
+        slot = tile_slots[r / job.h];  // prefetched for the tile's tokens (-1 when inactive)
+      else
+        slot = token < active ? p.slots[token] : -1;
       live = slot >= 0;
     }
     if (!__any_sync(0xffffffffu, live)) continue;
