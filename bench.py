@@ -570,6 +570,242 @@ def run_rotate_store(args):
     print(json.dumps(line), flush=True)
 
 
+def config4_state(device, seed=404):
+    """Config 4 (MTP verify): 32 requests with qlen 4 (1 + 3 draft tokens) and seq_len
+    ~ exp(U(ln 2048, ln 262144)) seeded; S=4, R=128, MTP=3; request 5's last draft has
+    a padded -1 slot and a 33rd, zero-length padded row closes the batch."""
+    from oscar_new_b200 import kernels
+    from oscar_new_b200.config import OscarConfig
+    from oscar_new_b200.layout import CacheLayout
+    from oscar_new_b200.synthetic import cache_stripes, plan_pages, rotation
+
+    gen = torch.Generator().manual_seed(seed)
+    u = torch.rand(32, generator=gen, dtype=torch.float64)
+    seqs = [int(math.exp(math.log(2048) + x * (math.log(262144) - math.log(2048)))) for x in u.tolist()]
+    seqs.append(0)
+    qlens = [4] * 32 + [0]
+    cfg = replace(OscarConfig(), sink_tokens=SINK, recent_tokens=RECENT, speculative_tokens=3)
+    layout = CacheLayout(BP, kv_heads=H, config=cfg)
+    plan = plan_pages(seqs, qlens, BP, seed=seed, max_reqs=34)
+    cache = cache_stripes(plan.num_pages, BP, H, device)
+    history, window = layout.tensor_views(cache)
+    rk, rv = rotation(1).bfloat16().to(device), rotation(2).bfloat16().to(device)
+    dgen = torch.Generator(device=device).manual_seed(seed)
+    chunk = 16384
+    for req, (sq, ql) in enumerate(zip(seqs, qlens)):
+        prefix = sq - ql
+        for s0 in range(0, prefix, chunk):
+            n = min(chunk, prefix - s0)
+            k = torch.randn(n, H, D, device=device, generator=dgen)
+            k[..., :8] *= 20
+            k = k.bfloat16()
+            v = torch.randn(n, H, D, device=device, generator=dgen).bfloat16()
+            slots = plan.slots_of(req, range(s0, s0 + n)).to(device)
+            counts = torch.tensor([1, n], dtype=torch.int32, device=device)
+            kernels.rotate_store(k, v, rk, rv, history, slots, counts, layout)
+            m1 = plan.meta(device)
+            m1.query_start_loc = torch.tensor([0, n], dtype=torch.int32, device=device)
+            m1.seq_lens = torch.tensor([s0 + n], dtype=torch.int32, device=device)
+            m1.block_tables = plan.block_tables[req : req + 1].to(device).contiguous()
+            m1.counts = counts
+            m1.max_num_reqs = 1
+            kernels.store_windows(k, v, window, m1, layout)
+    meta = plan.meta(device, cfg.queries_per_tile)
+    meta.slot_mapping[5 * 4 + 3] = -1
+    t = sum(qlens)
+    q = torch.randn(t, H * G, D, device=device, generator=dgen).bfloat16()
+    k = torch.randn(t, H, D, device=device, generator=dgen)
+    k[..., :8] *= 20
+    v = torch.randn(t, H, D, device=device, generator=dgen).bfloat16()
+    torch.cuda.synchronize(device)
+    hist_heads = 0
+    for sq, ql in zip(seqs, qlens):
+        prefix = sq - ql
+        sink_len = min(SINK, prefix)
+        hist_heads += H * max(0, max(sink_len, prefix - RECENT) - sink_len)
+    return dict(cfg=cfg, layout=layout, plan=plan, cache=cache, history=history, window=window, rk=rk, rv=rv,
+                meta=meta, q=q, k=k.bfloat16(), v=v, seqs=seqs, qlens=qlens, hist_token_heads=hist_heads)
+
+
+def run_mtp_verify(args):
+    from oscar_new_b200 import _lib, kernels
+    from oscar_new_b200.config import decode_split_cap
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    _lib.lib()
+    st = config4_state(device)
+    m = st["meta"]
+    t = st["q"].shape[0]
+    splits = decode_split_cap(32, H, 4, t, H * G)
+    out = torch.empty((t, H * G * D), dtype=torch.bfloat16, device=device)
+    scratch = kernels.DecodeScratch(t, H * G, splits, device)
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
+                              st["cfg"].queries_per_tile)
+        qrot = kernels.rotate_store(st["k"], st["v"], st["rk"], st["rv"], st["history"], m.slot_mapping, m.counts,
+                                    st["layout"], query=st["q"])
+        kernels.decode_attention(qrot, st["q"], st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                                 scale, splits, st["rv"], out, scratch)
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    qrot = kernels.rotate(st["q"], st["rk"])
+    for _ in range(3):
+        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"], scale,
+                                   splits, False)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for _ in range(args.steps):
+        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"], scale,
+                                   splits, False)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    kern_ms = e0.elapsed_time(e1) / args.steps
+    hist_bytes = st["hist_token_heads"] * HISTORY_BYTES_PER_TOKEN_HEAD
+    kv_tokens = sum(st["seqs"]) * H
+    peak, peak_kind = measured_peaks()
+    achieved = hist_bytes / (kern_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": kv_tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int2-kv/bf16", "data": "synthetic (seeded, config 4)",
+        "config": {"workload": "config4 MTP verify (qlen 4) paged INT2 decode attention layer",
+                   "requests": 32, "padded_rows": 1, "sum_seq_len": sum(st["seqs"]),
+                   "kv_splits": f"balanced per request, at most {splits}",
+                   "history_token_heads": st["hist_token_heads"], "history_bytes": hist_bytes,
+                   "l2": "inputs larger than L2", "us_per_layer": ms * 1e3},
+        "roofline": {"kernel": "history_attention_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm copy GB/s", "unit": "GB/s", "frac": achieved / peak,
+                     "us_per_launch": kern_ms * 1e3, "algorithmic_bytes_per_launch": hist_bytes, "traffic": None},
+        "gpu_launches": 6 * args.steps, "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_calibration(args):
+    """Config 5: 16 layers x 4 KV heads (6 query heads each), 16 segments x 1024 tokens,
+    channels 0-7 = 20 * Student-t(3); both passes, the covariance all-reduce and the
+    rank-0 eigensolve + publication.  Segments are sharded over ranks (strong scaling:
+    the job is fixed); one NCCL all-reduce in second_pass and one in finish."""
+    from oscar_new_b200 import _lib
+    from oscar_new_b200 import calibration_kernels as ck
+    from oscar_new_b200.calibration_worker import CalibrationSession
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        group = dist.group.WORLD
+    _lib.lib()
+    layers, segments, tokens = 16, 16, 1024
+    gen = torch.Generator(device=device).manual_seed(505)
+
+    def student(shape):
+        chi2 = torch.randn(*shape, 3, device=device, generator=gen).square().sum(-1)
+        return 20 * torch.randn(*shape, device=device, generator=gen) / (chi2 / 3).sqrt()
+
+    data = {}
+    for layer in range(layers):
+        for seg in range(segments):
+            if seg % world != rank:
+                continue
+            q = torch.randn(tokens, H * G, D, device=device, generator=gen)
+            k = torch.randn(tokens, H, D, device=device, generator=gen)
+            v = torch.randn(tokens, H, D, device=device, generator=gen)
+            for x in (q, k, v):
+                x[..., :8] = student(x[..., :8].shape)
+            data[(layer, seg)] = (q.bfloat16(), k.bfloat16(), v.bfloat16())
+    outdir = tempfile.mkdtemp(prefix="oscar_calib_")
+
+    def job():
+        s = CalibrationSession(range(layers), 10**9, device, H, G, shard="tokens", group=group)
+        for phase in (1, 2):
+            for (layer, _), (q, k, v) in data.items():
+                s.observe(layer, q.view(tokens, -1), k.view(tokens, -1), v.view(tokens, -1), tokens)
+            if phase == 1:
+                s.second_pass()
+        return s.finish(outdir, {"model_fingerprint": "synthetic-config5"}, 12)
+
+    for _ in range(1):
+        job()  # warm-up (first-call setup)
+    torch.cuda.synchronize(device)
+    times, info = [], None
+    steps = max(1, min(args.steps, 5))
+    for _ in range(steps):
+        if group is not None:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        info = job()
+        torch.cuda.synchronize(device)
+        times.append(time.perf_counter() - t0)
+    job_s = statistics.median(times)
+    if group is not None:
+        t = torch.tensor([job_s], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        job_s = float(t.item())
+    # component timings on this rank: Gram over one (layer, segment) and the eigensolve
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    q0 = next(iter(data.values()))[0]
+    cov = torch.zeros((D, D), dtype=torch.float32, device=device)
+    for _ in range(3):
+        ck.accumulate_gram(q0[:, :G], cov)
+    e0.record(stream)
+    for _ in range(20):
+        ck.accumulate_gram(q0[:, :G], cov)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    gram_ms = e0.elapsed_time(e1) / 20
+    gram_tflops = 2 * tokens * G * D * D / (gram_ms * 1e-3) / 1e12
+    stack = torch.randn(2 * layers, D, D, device=device)
+    stack = stack @ stack.transpose(-1, -2) / D
+    e0.record(stream)
+    _, _, einfo = ck.calibrated_rotations(stack)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    eig_ms = e0.elapsed_time(e1)
+    if rank == 0:
+        line = {
+            "metric": "calibration_job_seconds", "value": job_s, "unit": "s", "n_gpus": world, "steps": steps,
+            "warmup": 1, "ms_per_step": job_s * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16->fp32 (Gram), fp64 (Jacobi)", "data": "synthetic (seeded, config 5)",
+            "config": {"workload": "config5 calibration: 16 layers x 16 segments x 1024 tokens, both passes, "
+                                   "NCCL all-reduce, device Jacobi + U H P_br, checkpoint write",
+                       "layers": layers, "segments": segments, "tokens_per_segment": tokens, "kv_heads": H,
+                       "q_heads_per_kv": G, "shard": "tokens (segments round-robin over ranks)",
+                       "sweeps": info["sweeps"], "relative_off_diagonal": info["relative_off_diagonal"],
+                       "gram_us_per_1024x6_rows": gram_ms * 1e3, "gram_tflops": gram_tflops,
+                       "gram_frac_of_measured_bf16": gram_tflops / _measured_tflops(),
+                       "eigensolve_32_matrices_ms": eig_ms, "eigensolve_sweeps": einfo["sweeps"]},
+            "gpu_launches": None,
+        }
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def _measured_tflops(kind="bf16_tflops"):
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -626,8 +862,9 @@ def main():
     ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
     ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store"], default=None,
                     help="build the state, run 4 launches of the kernel (or 4 layer steps) and exit")
-    ap.add_argument("--workload", choices=["decode", "rotate-store"], default="decode",
-                    help="decode: config 3 (the headline); rotate-store: config 2")
+    ap.add_argument("--workload", choices=["decode", "rotate-store", "mtp-verify", "calibration"], default="decode",
+                    help="decode: config 3 (the headline); rotate-store: config 2; mtp-verify: config 4; "
+                         "calibration: config 5")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -639,6 +876,10 @@ def main():
         run_reference(args)
     elif args.workload == "rotate-store":
         run_rotate_store(args)
+    elif args.workload == "mtp-verify":
+        run_mtp_verify(args)
+    elif args.workload == "calibration":
+        run_calibration(args)
     else:
         run_gpu(args)
 

@@ -17,7 +17,7 @@ import os
 import torch
 from vllm.v1.attention.backend import AttentionBackend, AttentionImpl
 
-from .config import OscarConfig, choose_splits
+from .config import OscarConfig, decode_split_cap
 
 
 class OscarAttentionBackend(AttentionBackend):
@@ -148,7 +148,7 @@ class OscarAttentionImpl(AttentionImpl):
             return output
         qrot = kernels.rotate_store(key, value, self.rk, self.rv, self.history, meta.slot_mapping, meta.counts,
                                     meta.layout, query=query)
-        splits = choose_splits(meta.num_reqs, self.num_kv_heads, meta.max_query_len)
+        splits = decode_split_cap(meta.num_reqs, self.num_kv_heads, meta.max_query_len, n, self.num_heads)
         out = output.view(n, self.num_heads * self.head_size)
         kernels.decode_attention(qrot, query, key, value, self.history, self.window, meta, meta.layout,
                                  self.scale, splits, self.rv, out)

@@ -116,6 +116,20 @@ def choose_splits(num_requests: int, num_kv_heads: int, max_query_len: int) -> i
     return 8
 
 
+def decode_split_cap(num_requests: int, num_kv_heads: int, max_query_len: int, num_tokens: int,
+                     num_q_heads: int, scratch_bytes: int = 256 << 20) -> int:
+    """Most KV splits a decode / verify step may use.  The device balances splits per
+    request (a long request gets more, a short one fewer, all splits of similar
+    length), so the cap only bounds the fp32 split scratch [tokens, Hq, splits+1, 256]:
+    the reference policy (``choose_splits``) is the floor, raised up to 64 while the
+    scratch stays under ``scratch_bytes``."""
+    base = choose_splits(num_requests, num_kv_heads, max_query_len)
+    if max_query_len > 16:
+        return base
+    fit = scratch_bytes // max(num_tokens * num_q_heads * 256 * 4, 1) - 1
+    return max(base, min(64, fit))
+
+
 def percentile_selection(ratio: float, dim: int = 256):
     """Descending ranks (low, high) and weight of the linear quantile
     (reference ``config.py:92-97``).

@@ -26,7 +26,7 @@
 namespace oscar {
 
 constexpr int kStages = 4;
-constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxConsumerWarps = 8;  // wider CTAs spill the O accumulator
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kTwo24 = 16777216.0f;
 constexpr float kRescaleSlack = 3.0f;  // lazily re-base the running max (p <= 2^3)
@@ -52,7 +52,14 @@ struct HistParams {
   int32_t chunk_tokens;   // CT
   int32_t stage_bytes;
   int32_t *status;        // nullable error word
+  // balanced splits (decode path): a request of L history tokens uses
+  // clamp(ceil(L / span), 1, splits) splits, span = max(kMinSplitTokens,
+  // total history * head groups / target_ctas); empty splits write only lse = -inf
+  int32_t balanced;
+  int32_t target_ctas;
 };
+
+constexpr int kMinSplitTokens = 1024;
 
 struct TaskInfo {
   bool live;
@@ -178,13 +185,43 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
   const int h0 = blockIdx.z * P.heads_per_cta;
   const TaskInfo ti = load_task(task, P.tasks, P.task_count, P.qstarts, P.seq_lens, P.counts, g);
   if (!ti.live || ti.qlen <= 0) return;
-  const int rows_valid = min(g.query_tile, ti.qlen - ti.qoff) * g.group;
+  const int rows_valid = min(g.query_tile, ti.qoff < ti.qlen ? ti.qlen - ti.qoff : 0) * g.group;
   const int length = ti.recent_begin - ti.sink_len;
   const int tiles = (length + 31) / 32;
-  const int per_split = (tiles + P.splits - 1) / P.splits;
+  int nsplit = P.splits;
+  if (P.balanced) {
+    __shared__ int s_span;
+    if (warp == 0) {
+      int64_t total = 0;
+      const int nt = min(P.task_count[0], P.num_tasks);
+      for (int t2 = lane; t2 < nt; t2 += 32) {
+        const TaskInfo tj = load_task(t2, P.tasks, P.task_count, P.qstarts, P.seq_lens, P.counts, g);
+        if (tj.live && tj.qlen > 0) total += max(0, tj.recent_begin - tj.sink_len);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+      if (lane == 0) {
+        const int64_t span = (total * gridDim.z + P.target_ctas - 1) / max(P.target_ctas, 1);
+        s_span = (int)(span < kMinSplitTokens ? (int64_t)kMinSplitTokens : (span > (1 << 30) ? (int64_t)(1 << 30) : span));
+      }
+    }
+    __syncthreads();
+    nsplit = max(1, min(P.splits, (length + s_span - 1) / s_span));
+  }
+  const int per_split = (tiles + nsplit - 1) / nsplit;
   const int begin = split * per_split * 32;
   const int end = min((split + 1) * per_split * 32, length);
   const int lo = ti.sink_len + begin, hi = ti.sink_len + max(end, begin);  // absolute positions
+  if (P.balanced && hi <= lo) {
+    // unused split of a balanced launch: only the lse marker (the merge skips it)
+    for (int i = threadIdx.x; i < P.heads_per_cta * rows_valid; i += blockDim.x) {
+      const int hl = i / rows_valid, row = i % rows_valid;
+      const int tok = ti.qstart + ti.qoff + row / g.group;
+      const int qh = (h0 + hl) * g.group + row % g.group;
+      P.lse[((int64_t)tok * g.kv_heads * g.group + qh) * P.split_slots + split] = -INFINITY;
+    }
+    return;
+  }
   const int CT = P.chunk_tokens;
   const int first_chunk = lo / CT;
   const int nchunks = hi > lo ? (hi - 1) / CT - first_chunk + 1 : 0;
@@ -505,6 +542,9 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
     const int qh = head * g.group + row % g.group;
     const int64_t orow = ((int64_t)tok * g.kv_heads * g.group + qh) * P.split_slots + split;
     const bool any = L[r] > 0.f;
+    // lse (natural log): m is in log2 units
+    if (gi == 0) P.lse[orow] = any ? (mtot[r] * 0.69314718055994531f + logf(L[r])) : -INFINITY;
+    if (!any && P.balanced) continue;  // the merge skips -inf splits without reading them
     const float inv = any ? 1.0f / L[r] : 0.f;
     const float zterm = any ? Z[r] * inv : 0.f;
     float *dst = P.partials + orow * kDim + 32 * gi;
@@ -521,8 +561,6 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
         }
         *reinterpret_cast<float4 *>(dst + 16 * half + 4 * q4) = make_float4(v[0], v[1], v[2], v[3]);
       }
-    // lse (natural log): m is in log2 units
-    if (gi == 0) P.lse[orow] = any ? (mtot[r] * 0.69314718055994531f + logf(L[r])) : -INFINITY;
   }
 }
 
@@ -1063,9 +1101,19 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) 
   if (smem < 128 + xch) smem = 128 + xch;
   if (smem > 227 * 1024) return OSCAR_ERR_UNSUPPORTED;
   dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
-  if (P.consumers <= 8) return launch_history<8, NM>(P, grid, smem, stream);
-  if (P.consumers <= 12) return launch_history<12, NM>(P, grid, smem, stream);
-  return launch_history<16, NM>(P, grid, smem, stream);
+  return launch_history<kMaxConsumerWarps, NM>(P, grid, smem, stream);
+}
+
+// SM count of the current device (cached per device).
+static int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    cache[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+  }
+  return cache[dev];
 }
 
 static int raw_launch(const RawParams &P, int32_t num_tasks, cudaStream_t stream) {
@@ -1223,6 +1271,8 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     H.partials = scratch_partials, H.lse = scratch_lse, H.split_slots = splits + 1, H.splits = splits;
     H.geo = geo;
     H.scale_log2 = scale * kLog2e;
+    H.balanced = 1;
+    H.target_ctas = 8 * sm_count();
     int rc = history_launch(H, num_tasks, st);
     if (rc) return rc;
     RawParams R{};
