@@ -195,6 +195,19 @@ int oscar_accumulate_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int6
 int oscar_sst_weights(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1,
                       const float *q_cov, float *weights, float *total, void *stream);
 
+/* Grouped Gram: the h heads form `groups` equal groups of consecutive heads; group g
+ * accumulates into covs + g*65536 (rows of its heads only), weights as above (indexed
+ * by token * h + head).  One launch for all KV heads of a layer where the reference
+ * calls accumulate_gram per head (calibration_worker.py:75-82). */
+int oscar_accumulate_gram_grouped(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int32_t groups,
+                                  const float *weights, float *covs, void *stream);
+
+/* Per-head SST weights: head h's rows use q_covs + h*65536 and add into totals[h];
+ * weights is fp32 [n*h] indexed token * h + head.  Same arithmetic as
+ * oscar_sst_weights, one launch for all heads. */
+int oscar_sst_weights_per_head(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1,
+                               const float *q_covs, float *weights, float *totals, void *stream);
+
 /* out = x / max(denominator, 1e-30); the denominator is *device_denominator when
  * non-null, else host_denominator.  Reference :129-156. */
 int oscar_normalize(const float *x, int64_t numel, const float *device_denominator,

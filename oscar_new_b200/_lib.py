@@ -63,6 +63,8 @@ _SIGNATURES = {
     "oscar_decode_attention": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, P, P, Geometry, F32, I32, I32, P],
     "oscar_accumulate_gram": [P, I64, I32, I64, I64, P, P, P],
     "oscar_sst_weights": [P, I64, I32, I64, I64, P, P, P, P],
+    "oscar_accumulate_gram_grouped": [P, I64, I32, I64, I64, I32, P, P, P],
+    "oscar_sst_weights_per_head": [P, I64, I32, I64, I64, P, P, P, P],
     "oscar_normalize": [P, I64, P, F32, P, P],
     "oscar_jacobi_rotations": [P, I32, I32, F32, P, P, P, P],
     "oscar_decode_attention_noalloc": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P],

@@ -44,6 +44,44 @@ def accumulate_gram(x: torch.Tensor, covariance: torch.Tensor, weights: torch.Te
               None if w is None else w.data_ptr(), covariance.data_ptr(), _stream(x))
 
 
+def accumulate_gram_grouped(x: torch.Tensor, covariances: torch.Tensor, weights: torch.Tensor | None = None):
+    """``covariances[g] += sum over the rows of head group g`` (x [n, h, 256]; the h
+    heads split into ``covariances.shape[0]`` equal groups of consecutive heads) in one
+    launch; optional per-row weights [n * h] (or [n, h])."""
+    _cuda(x, covariances, weights)
+    groups = covariances.shape[0]
+    if covariances.dtype != torch.float32 or covariances.shape[1:] != (256, 256) or not covariances.is_contiguous():
+        raise ValueError("covariances must be contiguous fp32 [groups, 256, 256]")
+    n, h, d = x.shape
+    if d != 256 or h % groups:
+        raise ValueError("head_dim must be 256 and the heads must split evenly into the groups")
+    if x.dtype != torch.bfloat16 or x.stride(2) != 1 or x.stride(0) % 8 or x.stride(1) % 8 or x.data_ptr() % 16:
+        x = x.to(torch.bfloat16).contiguous()
+    w = None
+    if weights is not None:
+        w = weights.float().contiguous().view(-1)
+        if w.numel() != n * h:
+            raise ValueError("weights must have one entry per (token, head) row")
+    _lib.call("oscar_accumulate_gram_grouped", x.data_ptr(), n, h, x.stride(0), x.stride(1), groups,
+              None if w is None else w.data_ptr(), covariances.data_ptr(), _stream(x))
+
+
+def sst_weights_per_head(key: torch.Tensor, q_covariances: torch.Tensor, totals: torch.Tensor):
+    """Per-head ``w = max(k C_h k^T, 0)`` (key [n, h, 256], q_covariances [h, 256, 256])
+    and ``totals[h] += sum w``; returns w as fp32 [n * h] (token-major)."""
+    _cuda(key, q_covariances, totals)
+    n, h, d = key.shape
+    if q_covariances.shape != (h, 256, 256) or totals.numel() != h or not totals.is_contiguous():
+        raise ValueError("one covariance and one total per head")
+    if key.dtype != torch.bfloat16:
+        key = key.to(torch.bfloat16)
+    c = q_covariances.float().contiguous()
+    weights = torch.empty(n * h, device=key.device, dtype=torch.float32)
+    _lib.call("oscar_sst_weights_per_head", key.data_ptr(), n, h, key.stride(0), key.stride(1), c.data_ptr(),
+              weights.data_ptr(), totals.data_ptr(), _stream(key))
+    return weights
+
+
 def sst_weights(key: torch.Tensor, q_covariance: torch.Tensor, total_weight: torch.Tensor):
     """``w_t = max(k_t C k_t^T, 0)`` per row and ``total_weight += sum w``
     (reference calibration_kernels.py:109-126; any number of KV heads)."""
@@ -70,7 +108,7 @@ def normalize(x: torch.Tensor, denominator):
 
 
 def calibrated_rotations(covariances: torch.Tensor, max_sweeps: int = 12, tolerance: float = 1e-6,
-                         refine: float = 1e-10):
+                         refine: float = 1e-7):
     """Batched cyclic Jacobi + ``U H P_br`` (reference :287-327).
 
     Returns ``(rotations [B,256,256], eigenvalues [B,256], info)``; raises like the
@@ -78,7 +116,9 @@ def calibrated_rotations(covariances: torch.Tensor, max_sweeps: int = 12, tolera
     reference's ``max|off| / max|diag| < tolerance``; the sweeps continue (within
     ``max_sweeps``) down to ``refine``, because with a wide spectrum an off-diagonal
     left at ``1e-6 * max|diag|`` still moves the small, closely spaced eigenvalues by
-    about ``off^2 / gap`` (1e-4 relative on covariances with outlier channels).
+    about ``off^2 / gap`` (1e-4 relative on covariances with outlier channels; ~1e-6
+    at 1e-7).  The reference's skip rule (no rotation once |a_pq| < 1e-8 (|a_pp| +
+    |a_qq|)) keeps the residual near 1e-8, so tighter targets only burn sweeps.
     """
     _cuda(covariances)
     if covariances.dtype != torch.float32:

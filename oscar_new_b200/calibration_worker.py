@@ -108,15 +108,13 @@ class CalibrationSession:
             return
         h, g = self.heads, self.group_size
         if self.phase == 1:
-            q = query[:take].reshape(take, h * g, DIM)
-            for head in range(h):
-                self.ops.accumulate_gram(q[:, head * g : (head + 1) * g], state["q_sum"][head])
+            # one launch: KV head j accumulates its G query heads into q_sum[j]
+            self.ops.accumulate_gram_grouped(query[:take].reshape(take, h * g, DIM), state["q_sum"])
         else:
             k = key[:take].reshape(take, h, DIM)
             v = value[:take].reshape(take, h, DIM)
-            for head in range(h):
-                w = self.ops.sst_weights(k[:, head : head + 1], state["q_cov"][head], state["weight_sum"][head : head + 1])
-                self.ops.accumulate_gram(v[:, head : head + 1], state["v_sum"][head], w)
+            w = self.ops.sst_weights_per_head(k, state["q_cov"], state["weight_sum"])
+            self.ops.accumulate_gram_grouped(v, state["v_sum"], w)
         state[counter] += take
 
     def second_pass(self):

@@ -10,6 +10,8 @@
 // spin), and the sweep count is bounded.
 #include <cooperative_groups.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -21,20 +23,23 @@ namespace oscar {
 // output tile (blockIdx.y in 0..3) over a chunk of rows (blockIdx.x); fp32 partial
 // tile reduced into cov with vector atomics.
 // ----------------------------------------------------------------------------
-constexpr int kGramRows = 32;     // rows per pipeline step
-constexpr int kGramChunk = 2048;  // rows per CTA
+constexpr int kGramRows = 32;  // rows per pipeline step
 
+// blockIdx.z = output group: heads [z*hpg, (z+1)*hpg) accumulate into cov + z*D*D;
+// blockIdx.x = a chunk of `chunk` rows (token, head-in-group) of that group.
 __global__ void __launch_bounds__(256) gram_kernel(const __nv_bfloat16 *__restrict__ x, int64_t n, int32_t h,
                                                    int64_t xs0, int64_t xs1, const float *__restrict__ w,
-                                                   float *__restrict__ cov) {
+                                                   float *__restrict__ cov_base, int32_t hpg, int32_t chunk) {
   __shared__ __align__(16) __nv_bfloat16 si[kGramRows * 128];   // x[row][i-range]
   __shared__ __align__(16) __nv_bfloat16 sj[kGramRows * 128];   // x[row][j-range] (or w*x hi)
   __shared__ __align__(16) __nv_bfloat16 sjl[kGramRows * 128];  // w*x lo part
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ti = blockIdx.y >> 1, tj = blockIdx.y & 1;
-  const int64_t rows = n * h;
-  const int64_t r0 = (int64_t)blockIdx.x * kGramChunk;
-  const int64_t r1 = min(rows, r0 + kGramChunk);
+  const int group = blockIdx.z;
+  float *cov = cov_base + (size_t)group * kDim * kDim;
+  const int64_t rows = n * hpg;
+  const int64_t r0 = (int64_t)blockIdx.x * chunk;
+  const int64_t r1 = min(rows, r0 + chunk);
   const int wm = warp >> 2, wn = warp & 3;  // warp tile 64 (i) x 32 (j)
   float acc[4][4][4];
 #pragma unroll
@@ -53,10 +58,12 @@ __global__ void __launch_bounds__(256) gram_kernel(const __nv_bfloat16 *__restri
       uint4 vi = make_uint4(0, 0, 0, 0), vj = vi;
       float wt = 0.f;
       if (row < r1) {
-        const __nv_bfloat16 *src = x + (row / h) * xs0 + (row % h) * xs1;
+        const int64_t t = row / hpg;
+        const int hh = group * hpg + (int)(row % hpg);
+        const __nv_bfloat16 *src = x + t * xs0 + hh * xs1;
         vi = *reinterpret_cast<const uint4 *>(src + ti * 128 + ch * 8);
         vj = *reinterpret_cast<const uint4 *>(src + tj * 128 + ch * 8);
-        if (weighted) wt = w[row];
+        if (weighted) wt = w[t * h + hh];
       }
       const int sw = ((ch ^ (r & 7)) << 3);
       *reinterpret_cast<uint4 *>(si + r * 128 + sw) = vi;
@@ -123,21 +130,28 @@ __global__ void __launch_bounds__(256) gram_kernel(const __nv_bfloat16 *__restri
 // SST weights: w_t = max(k_t C k_t^T, 0); total += sum w.  CTA = 32 rows; thread j
 // owns column j of y = K C, fp32 FMAs (reference keeps this product in fp32).
 // ----------------------------------------------------------------------------
+// per_head = 0: rows (token, head) of all heads against one C and one total;
+// per_head = 1: blockIdx.y = head, rows are that head's tokens against C[head], total[head].
 __global__ void __launch_bounds__(256) sst_kernel(const __nv_bfloat16 *__restrict__ k, int64_t n, int32_t h,
-                                                  int64_t ks0, int64_t ks1, const float *__restrict__ c,
-                                                  float *__restrict__ w, float *__restrict__ total) {
+                                                  int64_t ks0, int64_t ks1, const float *__restrict__ c_base,
+                                                  float *__restrict__ w, float *__restrict__ total_base,
+                                                  int32_t per_head) {
   __shared__ __align__(16) float sk[kDim][32];  // [i][row]
   __shared__ float red[8][32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t rows = n * h;
+  const int head = per_head ? (int)blockIdx.y : 0;
+  const float *c = c_base + (size_t)head * kDim * kDim;
+  float *total = total_base + head;
+  const int64_t rows = per_head ? n : n * h;
   const int64_t r0 = (int64_t)blockIdx.x * 32;
+  auto out_index = [&](int64_t row) { return per_head ? row * h + head : row; };
   for (int e = tid; e < 32 * kDim; e += 256) {
     const int r = e / kDim, i = e % kDim;
     const int64_t row = r0 + r;
     float v = 0.f;
     if (row < rows) {
-      const uint16_t bits = reinterpret_cast<const uint16_t *>(k + (row / h) * ks0 + (row % h) * ks1)[i];
-      v = bf16_bits_to_float(bits);
+      const __nv_bfloat16 *src = per_head ? k + row * ks0 + head * ks1 : k + (row / h) * ks0 + (row % h) * ks1;
+      v = bf16_bits_to_float(reinterpret_cast<const uint16_t *>(src)[i]);
     }
     sk[i][r] = v;
   }
@@ -173,7 +187,7 @@ __global__ void __launch_bounds__(256) sst_kernel(const __nv_bfloat16 *__restric
     for (int q = 0; q < 8; ++q) v += red[q][lane];
     v = fmaxf(v, 0.f);
     const bool ok = r0 + lane < rows;
-    if (ok) w[r0 + lane] = v;
+    if (ok) w[out_index(r0 + lane)] = v;
     float s = ok ? v : 0.f;
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -205,13 +219,19 @@ struct JacobiSmem {
   int flag[2];
 };
 
+// x mod (D-1) for x in (-(D-1), 2(D-1)): two conditional corrections, no division.
+OSCAR_DEVINL int mod_dm1(int x) {
+  x += x < 0 ? (kDim - 1) : 0;
+  return x >= kDim - 1 ? x - (kDim - 1) : x;
+}
+
 OSCAR_DEVINL void round_pair(int j, int r, int &p, int &q) {
   if (j == 0) {
     p = kDim - 1;
     q = r;
   } else {
-    p = (r + j) % (kDim - 1);
-    q = (r - j + kDim - 1) % (kDim - 1);
+    p = mod_dm1(r + j);
+    q = mod_dm1(r - j);
   }
 }
 
@@ -281,15 +301,16 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
       }
       cluster.sync();
       // (3) fetch each local row's partner row (possibly remote), then (4) row rotations
-      for (int e = tid; e < kJRows * kDim; e += kJThreads) {
-        const int lr = e / kDim, col = e % kDim;
+      // 16-byte loads: a local row is 256 doubles = 128 double2; one warp per 4 rows
+      for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
+        const int lr = e / (kDim / 2), c2 = e % (kDim / 2);
         const int x = row0 + lr;
         int y;
         if (x == kDim - 1) y = r;
         else if (x == r) y = kDim - 1;
-        else y = ((2 * r - x) % (kDim - 1) + (kDim - 1)) % (kDim - 1);
+        else y = mod_dm1(mod_dm1(2 * r - x));
         const JacobiSmem *own = cluster.map_shared_rank(&S, y / kJRows);
-        S.tmp[lr][col] = own->a[y % kJRows][col];
+        reinterpret_cast<double2 *>(S.tmp[lr])[c2] = reinterpret_cast<const double2 *>(own->a[y % kJRows])[c2];
       }
       cluster.sync();
       for (int e = tid; e < kJRows * kDim; e += kJThreads) {
@@ -301,11 +322,11 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
         } else if (x == r) {
           j = 0, isp = 0;
         } else {
-          const int jp = ((x - r) % (kDim - 1) + (kDim - 1)) % (kDim - 1);  // x = (r + jp) mod (D-1)
+          const int jp = mod_dm1(x - r);  // x = (r + jp) mod (D-1)
           if (jp >= 1 && jp < kDim / 2) {
             j = jp, isp = 1;
           } else {
-            j = ((r - x) % (kDim - 1) + (kDim - 1)) % (kDim - 1), isp = 0;  // x = (r - j) mod (D-1)
+            j = mod_dm1(r - x), isp = 0;  // x = (r - j) mod (D-1)
           }
         }
         const double c = S.cs[j][0], s = S.cs[j][1];
@@ -426,17 +447,32 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
 
 using namespace oscar;
 
-extern "C" int oscar_accumulate_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1,
-                                     const float *weights, float *cov, void *stream) {
-  if (n < 0 || h <= 0 || !cov) return OSCAR_ERR_INVALID;
+static int launch_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int32_t groups,
+                       const float *weights, float *cov, void *stream) {
+  if (n < 0 || h <= 0 || groups <= 0 || h % groups || !cov) return OSCAR_ERR_INVALID;
   if (n == 0) return OSCAR_OK;
   if (!x || (reinterpret_cast<uintptr_t>(x) & 15) || xs0 % 8 || xs1 % 8) return OSCAR_ERR_INVALID;
-  const int64_t rows = n * h;
-  dim3 grid((unsigned)((rows + kGramChunk - 1) / kGramChunk), 4);
+  const int hpg = h / groups;
+  const int64_t rows = n * hpg;
+  // chunks sized so that the launch covers about two waves of 148 SMs
+  const int64_t want = std::max<int64_t>(1, (2 * 148 + 4 * groups - 1) / (4 * groups));
+  int64_t chunk = (rows + want - 1) / want;
+  chunk = std::max<int64_t>(256, std::min<int64_t>(4096, (chunk + kGramRows - 1) / kGramRows * kGramRows));
+  dim3 grid((unsigned)((rows + chunk - 1) / chunk), 4, (unsigned)groups);
   gram_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16 *>(x), n, h, xs0, xs1,
-                                                      weights, cov);
+                                                      weights, cov, hpg, (int32_t)chunk);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
+}
+
+extern "C" int oscar_accumulate_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1,
+                                     const float *weights, float *cov, void *stream) {
+  return launch_gram(x, n, h, xs0, xs1, 1, weights, cov, stream);
+}
+
+extern "C" int oscar_accumulate_gram_grouped(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1,
+                                             int32_t groups, const float *weights, float *covs, void *stream) {
+  return launch_gram(x, n, h, xs0, xs1, groups, weights, covs, stream);
 }
 
 extern "C" int oscar_sst_weights(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1, const float *q_cov,
@@ -446,7 +482,19 @@ extern "C" int oscar_sst_weights(const void *key, int64_t n, int32_t h, int64_t 
   if (!key) return OSCAR_ERR_INVALID;
   const int64_t rows = n * h;
   sst_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16 *>(key), n, h, ks0, ks1, q_cov, weights, total);
+      reinterpret_cast<const __nv_bfloat16 *>(key), n, h, ks0, ks1, q_cov, weights, total, 0);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
+extern "C" int oscar_sst_weights_per_head(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1,
+                                          const float *q_covs, float *weights, float *totals, void *stream) {
+  if (n < 0 || h <= 0 || !q_covs || !weights || !totals) return OSCAR_ERR_INVALID;
+  if (n == 0) return OSCAR_OK;
+  if (!key) return OSCAR_ERR_INVALID;
+  dim3 grid((unsigned)((n + 31) / 32), (unsigned)h);
+  sst_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16 *>(key), n, h, ks0, ks1,
+                                                     q_covs, weights, totals, 1);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
 }

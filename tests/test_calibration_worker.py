@@ -33,6 +33,21 @@ class CpuOps:
         return w
 
     @staticmethod
+    def accumulate_gram_grouped(x, covs, weights=None):
+        groups = covs.shape[0]
+        per = x.shape[1] // groups
+        w = None if weights is None else weights.reshape(x.shape[0], x.shape[1])
+        for gi in range(groups):
+            sl = slice(gi * per, (gi + 1) * per)
+            CpuOps.accumulate_gram(x[:, sl], covs[gi], None if w is None else w[:, sl])
+
+    @staticmethod
+    def sst_weights_per_head(k, q_covs, totals):
+        w = torch.stack([co.sst_weights(k[:, j : j + 1], q_covs[j]).float() for j in range(k.shape[1])], 1)
+        totals += w.sum(0)
+        return w.reshape(-1)
+
+    @staticmethod
     def normalize(x, denominator):
         if isinstance(denominator, torch.Tensor):
             return x / denominator.clamp_min(1e-30)
