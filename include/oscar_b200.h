@@ -148,7 +148,9 @@ int oscar_unpack(const uint8_t *history, const int64_t *slots, int64_t n, oscar_
  * split-KV attention (rotated space), BF16 sink/recent/current attention, split LSE
  * merge, inverse V rotation (hrot @ Rv^T) and path merge into `output` (bf16
  * [n, Hq*256]), then the window store of the current K/V.  Scratch: fp32 partials
- * [n*Hq*(splits+1)*256] and lse [n*Hq*(splits+1)] supplied by the caller.
+ * [n*Hq*(splits+1)*256] and lse [n*Hq*(splits+1)] supplied by the caller.  `splits`
+ * (1..64) is the most splits a request may use: each request gets a number of splits
+ * proportional to its history, so that every split covers a similar span.
  * Replaces reference backend.py:195-226 (attention_partials x2, merge_splits,
  * rotate(hrot, Rv^T), merge_paths, store_windows). */
 int oscar_decode_attention(const void *qrot, const void *query, int64_t qs0, int64_t qs1,

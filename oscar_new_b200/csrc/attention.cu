@@ -886,21 +886,41 @@ __global__ void __launch_bounds__(kFinThreads) finalize_kernel(FinalParams P) {
     const int r = warp * (kFinRows / 4) + i;
     const int64_t row = row0 + r;
     const bool valid = row < P.rows && row / P.hq < active;
-    float m = -INFINITY;
-    for (int s = 0; s < P.splits; ++s) m = fmaxf(m, valid ? P.lse[row * P.split_slots + s] : -INFINITY);
+    // lane s holds split s's lse (splits <= 64: two per lane); warp max / weights
+    const float *lrow = P.lse + row * P.split_slots;
+    const float l0 = valid && lane < P.splits ? lrow[lane] : -INFINITY;
+    const float l1 = valid && lane + 32 < P.splits ? lrow[lane + 32] : -INFINITY;
+    float m = fmaxf(l0, l1);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float safe = m == -INFINITY ? 0.f : m;
+    const float w0 = expf(l0 - safe), w1 = expf(l1 - safe);
+    float den = w0 + w1;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    float den = 0.f;
-    for (int s = 0; s < P.splits; ++s) {
-      const float l = valid ? P.lse[row * P.split_slots + s] : -INFINITY;
-      const float w = expf(l - safe);
-      den += w;
-      if (w != 0.f) {
-        const float4 *src = reinterpret_cast<const float4 *>(P.partials + (row * P.split_slots + s) * kDim + lane * 8);
-        const float4 x0 = src[0], x1 = src[1];
-        acc[0] = fmaf(w, x0.x, acc[0]), acc[1] = fmaf(w, x0.y, acc[1]), acc[2] = fmaf(w, x0.z, acc[2]);
-        acc[3] = fmaf(w, x0.w, acc[3]), acc[4] = fmaf(w, x1.x, acc[4]), acc[5] = fmaf(w, x1.y, acc[5]);
-        acc[6] = fmaf(w, x1.z, acc[6]), acc[7] = fmaf(w, x1.w, acc[7]);
+    // four splits per group: all loads of the group are in flight before any is used
+    for (int s0 = 0; s0 < P.splits; s0 += 4) {
+      float w[4];
+      float4 x[4][2];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int sp = s0 + u;
+        const float ws = __shfl_sync(0xffffffffu, sp < 32 ? w0 : w1, sp & 31);
+        w[u] = sp < P.splits ? ws : 0.f;
+        if (w[u] != 0.f) {
+          const float4 *src = reinterpret_cast<const float4 *>(P.partials + (row * P.split_slots + sp) * kDim + lane * 8);
+          x[u][0] = src[0], x[u][1] = src[1];
+        } else {
+          x[u][0] = x[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc[0] = fmaf(w[u], x[u][0].x, acc[0]), acc[1] = fmaf(w[u], x[u][0].y, acc[1]);
+        acc[2] = fmaf(w[u], x[u][0].z, acc[2]), acc[3] = fmaf(w[u], x[u][0].w, acc[3]);
+        acc[4] = fmaf(w[u], x[u][1].x, acc[4]), acc[5] = fmaf(w[u], x[u][1].y, acc[5]);
+        acc[6] = fmaf(w[u], x[u][1].z, acc[6]), acc[7] = fmaf(w[u], x[u][1].w, acc[7]);
       }
     }
     const float inv = 1.0f / fmaxf(den, 1e-30f);
@@ -1249,7 +1269,8 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
                                       const void *rv, float *scratch_partials, float *scratch_lse, void *output,
                                       oscar_geometry geo, float scale, int32_t splits, int32_t window_programs,
                                       void *stream) {
-  if (!geo_ok(geo) || splits <= 0 || num_tasks < 0 || n < 0 || window_programs < 0) return OSCAR_ERR_INVALID;
+  if (!geo_ok(geo) || splits <= 0 || splits > 64 || num_tasks < 0 || n < 0 || window_programs < 0)
+    return OSCAR_ERR_INVALID;  // the fused merge holds at most 64 split LSEs per row in one warp
   if (n == 0) return OSCAR_OK;
   if (!qrot || !query || !key || !value || !history || !window || !qstarts || !seq_lens || !table || !counts ||
       !tasks || !task_count || !rv || !scratch_partials || !scratch_lse || !output)
