@@ -3,10 +3,12 @@
 // BF16 window store (:544-620) and the compact task table (:222-287).
 //
 // History kernel (INT2, rotated space).  One CTA = one (task, split, head group).
-// A producer warp streams 128-token kernel blocks of the paged K stripe into a
-// 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk, mbarrier
-// completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast).
-// Consumer warps own (KV head, 8 query rows) units and 16-token m-tiles.
+// Lane 0 of warp 0 streams chunks of the paged K stripe (at most one 128-token kernel
+// block) into a 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk,
+// mbarrier completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast),
+// between its own chunks.  The 8 warps own (KV head, 8 query rows) units and 16-token
+// m-tiles; with no separate producer warp each thread may hold up to 255 registers,
+// which keeps four independent accumulators per code sum.
 //
 // Dequantisation is factored out of the MMA: k = c*s + z per token, so
 //   q.k   = s * (q.c) + z * sum(q)          and   sum_t p_t v_t = sum_t (p_t s_t) c_t + sum_t p_t z_t.
@@ -177,7 +179,7 @@ OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
 }
 
 template <int MAXW, int NM>
-__global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(HistParams P) {
+__global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   const oscar_geometry &g = P.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -240,34 +242,41 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
 
   const int hpc = P.heads_per_cta;
   const int token_bytes = hpc * g.slot_bytes;
-  if (warp == P.consumers) {
-    // ---------------- producer warp ----------------
-    if (lane == 0) {
-      const int32_t *trow = P.table + (int64_t)ti.req * g.table_stride;
-      for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kStages;
-        if (c >= kStages && !mbar_wait_bounded(&empty[s], ((c / kStages) - 1) & 1)) {
-          if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
-          break;
-        }
-        const int pos = (first_chunk + c) * CT;
-        const int64_t slot0 = (int64_t)trow[pos / kKernelBlock] * kKernelBlock + pos % kKernelBlock;
-        const uint8_t *src = P.history + (slot0 / g.block_tokens) * g.page_bytes +
-                             ((slot0 % g.block_tokens) * g.kv_heads + h0) * (int64_t)g.slot_bytes;
-        const uint32_t dst = smem_u32(stages + s * P.stage_bytes);
-        mbar_arrive_expect_tx(&full[s], CT * token_bytes);
-        if (hpc == g.kv_heads) {
-          bulk_copy_g2s(dst, src, CT * token_bytes, &full[s]);
-        } else {
-          for (int tk = 0; tk < CT; ++tk)
-            bulk_copy_g2s(dst + tk * token_bytes, src + (int64_t)tk * g.kv_heads * g.slot_bytes, token_bytes,
-                          &full[s]);
-        }
-      }
+  // Copies are issued by lane 0 of warp 0 between its own chunks: chunk c + kStages - 1
+  // as soon as the consumers have released its stage (non-blocking probe), and chunk c
+  // at the latest before warp 0 needs it (bounded blocking wait).  Keeping the CTA at
+  // 8 warps (2 per scheduler) leaves each thread up to 255 registers.
+  const int32_t *trow = P.table + (int64_t)ti.req * g.table_stride;
+  int issued = 0;
+  auto issue_one = [&](int c) {
+    const int s = c % kStages;
+    const int pos = (first_chunk + c) * CT;
+    const int64_t slot0 = (int64_t)trow[pos / kKernelBlock] * kKernelBlock + pos % kKernelBlock;
+    const uint8_t *src = P.history + (slot0 / g.block_tokens) * g.page_bytes +
+                         ((slot0 % g.block_tokens) * g.kv_heads + h0) * (int64_t)g.slot_bytes;
+    const uint32_t dst = smem_u32(stages + s * P.stage_bytes);
+    mbar_arrive_expect_tx(&full[s], CT * token_bytes);
+    if (hpc == g.kv_heads) {
+      bulk_copy_g2s(dst, src, CT * token_bytes, &full[s]);
+    } else {
+      for (int tk = 0; tk < CT; ++tk)
+        bulk_copy_g2s(dst + tk * token_bytes, src + (int64_t)tk * g.kv_heads * g.slot_bytes, token_bytes, &full[s]);
     }
-    return;
-  }
-  if (warp > P.consumers) return;
+  };
+  // returns false when a bounded wait for a free stage gave up
+  auto pump = [&](int c) -> bool {
+    while (issued <= c && issued < nchunks) {
+      if (issued >= kStages && !mbar_wait_bounded(&empty[issued % kStages], ((issued / kStages) - 1) & 1))
+        return false;
+      issue_one(issued++);
+    }
+    while (issued < nchunks && issued < c + kStages) {
+      if (issued >= kStages && !mbar_test(&empty[issued % kStages], ((issued / kStages) - 1) & 1)) break;
+      issue_one(issued++);
+    }
+    return true;
+  };
+  if (warp >= P.consumers) return;
 
   // ---------------- consumer warps ----------------
   const int unit = warp % P.units, sub = warp / P.units;
@@ -292,6 +301,15 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
 #pragma unroll 1
   for (int c = 0; c < nchunks && ok; ++c) {
     const int s = c % kStages;
+    if (warp == 0) {
+      bool pumped = true;
+      if (lane == 0) pumped = pump(c);
+      if (!__shfl_sync(0xffffffffu, (int)pumped, 0)) {
+        ok = false;
+        if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
+        break;
+      }
+    }
     if (!mbar_wait_bounded(&full[s], (c / kStages) & 1)) {
       ok = false;
       if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
@@ -320,11 +338,13 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
         kaw[j][0] = ka.x, kaw[j][1] = ka.y, kaw[j][2] = ka.z, kaw[j][3] = ka.w;
         kbw[j][0] = kb.x, kbw[j][1] = kb.y, kbw[j][2] = kb.z, kbw[j][3] = kb.w;
       }
-      float sc[NM][4], sd[NM][4];
+      float sc[NM][4][4];  // [m-tile][bit position p][fragment]: four independent HMMA chains
 #pragma unroll
       for (int j = 0; j < NM; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[j][e] = sd[j][e] = 0.f;
+        for (int p = 0; p < 4; ++p)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[j][p][e] = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
 #pragma unroll
@@ -332,8 +352,8 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
           const uint32_t msk = 0x00030003u << (2 * p);
 #pragma unroll
           for (int j = 0; j < NM; ++j) {
-            mma_f16_16816((p & 1) ? sd[j] : sc[j], kaw[j][i] & msk, kbw[j][i] & msk, (kaw[j][i] >> 8) & msk,
-                          (kbw[j][i] >> 8) & msk, Q.qf[4 * i + p][0], Q.qf[4 * i + p][1]);
+            mma_f16_16816(sc[j][p], kaw[j][i] & msk, kbw[j][i] & msk, (kaw[j][i] >> 8) & msk, (kbw[j][i] >> 8) & msk,
+                          Q.qf[4 * i + p][0], Q.qf[4 * i + p][1]);
           }
         }
       }
@@ -389,7 +409,7 @@ __global__ void __launch_bounds__(32 * (MAXW + 1), 1) history_attention_kernel(H
           const int r = e & 1;
           const float ha = 0.5f * kc.a;
           float dot = kc.v0 * Q.qsum[r];
-          dot = fmaf((kc.d1 + ha) * kTwo24, sc[j][e] + sd[j][e], dot);
+          dot = fmaf((kc.d1 + ha) * kTwo24, (sc[j][0][e] + sc[j][1][e]) + (sc[j][2][e] + sc[j][3][e]), dot);
           dot = fmaf(-ha * Q.qscale[r], (float)acc_a[j][e], dot);
           dot = fmaf(kc.b * Q.qscale[r], (float)acc_c[j][e], dot);
           lg[j][e] = ((e < 2) ? va[j] : vb[j]) ? dot * sl2 : -INFINITY;
@@ -1091,7 +1111,7 @@ static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStrea
       return OSCAR_ERR_LAUNCH;
     configured = smem;
   }
-  history_attention_kernel<MAXW, NM><<<grid, 32 * (P.consumers + 1), smem, stream>>>(P);
+  history_attention_kernel<MAXW, NM><<<grid, 32 * P.consumers, smem, stream>>>(P);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
 }

@@ -169,6 +169,18 @@ OSCAR_DEVINL bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
   return ok != 0;
 }
 
+// Non-blocking probe: has the phase with this parity completed?
+OSCAR_DEVINL bool mbar_test(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, "
+      "p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
 // Spin on an mbarrier phase with an iteration limit.  Returns false on timeout; the
 // caller records the error and stops consuming (never an unbounded hang).
 constexpr uint32_t kWaitLimit = 1u << 20;
