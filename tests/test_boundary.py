@@ -77,6 +77,15 @@ def test_split_policy_and_bad_config():
             replace(OscarConfig(), **kwargs)
 
 
+def test_decode_split_cap_bounds_the_scratch():
+    from oscar_new_b200.config import decode_split_cap
+
+    assert decode_split_cap(32, 4, 4, 128, 24) == 64  # 200 MB of split scratch
+    assert decode_split_cap(256, 4, 4, 1024, 24) == 9  # capped by the 256 MiB budget
+    assert decode_split_cap(2048, 4, 4, 8192, 24) == 8  # never below the reference policy
+    assert decode_split_cap(1, 1, 900, 900, 6) == 1  # prefill keeps one split
+
+
 def test_config_reads_reference_environment_names(monkeypatch):
     monkeypatch.setenv("VLLM_OSCAR_SINK_TOKENS", "4")
     monkeypatch.setenv("VLLM_OSCAR_RECENT_TOKENS", "128")

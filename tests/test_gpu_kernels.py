@@ -337,6 +337,8 @@ def test_attention_partials_match_reference_kernel(cuda_lib, index):
         ("prefill_chunk", [1700], [900], 6, 1, make_config(64, 256, 3), 1),
         ("empty_history", [4], [4], 6, 1, make_config(64, 256, 3), 32),
         ("ragged_overlap", [69, 263], [4, 3], 6, 1, make_config(64, 256, 3), 16),
+        # skewed lengths: balanced splits give the long request most of the 64 splits
+        ("skewed_balanced", [140, 9000, 333, 2, 1500], [4, 4, 1, 2, 4], 24, 4, make_config(4, 128, 3), 64),
     ],
 )
 def test_decode_step_matches_hybrid_reference(cuda_lib, name, seq, qlen, hq, h, cfg, splits):
