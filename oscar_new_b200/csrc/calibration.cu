@@ -301,7 +301,9 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
       }
       cluster.sync();
       // (3) fetch each local row's partner row (possibly remote), then (4) row rotations
-      // 16-byte loads: a local row is 256 doubles = 128 double2; one warp per 4 rows
+      // 16-byte loads: a local row is 256 doubles = 128 double2; the 16 remote loads of
+      // a thread are independent and unrolled so that they are in flight together
+#pragma unroll
       for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
         const int lr = e / (kDim / 2), c2 = e % (kDim / 2);
         const int x = row0 + lr;
