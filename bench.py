@@ -128,53 +128,70 @@ LAUNCHES_PER_STEP = 6  # tasks, rotate+store, history, raw, finalize, window sto
 
 
 class ClockSampler:
+    """nvidia-smi samples (every 20 ms) of this GPU's SM clock and throttle reasons;
+    `mark()` brackets the timed region and `summary()` keeps the samples inside it."""
+
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.path = None
+        self.window = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         time.sleep(0.3)
         return self
 
+    def mark(self, start, end):
+        self.window = (start, end)
+
     def __exit__(self, *exc):
+        time.sleep(0.05)
         if self.proc is not None:
             self.proc.terminate()
             self.proc.wait(timeout=5)
 
     def summary(self):
+        import datetime
+
         if not self.path or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        samples = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((ts, float(parts[2]), float(parts[3]),
+                                {n for n, v in zip(names, parts[6:10]) if v.lower() == "active"}))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
         os.unlink(self.path)
-        if not sm:
+        if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = samples
+        where = "timed region"
+        if self.window is not None:
+            lo, hi = self.window
+            inside = [x for x in samples if lo <= x[0] <= hi]
+            if not inside:  # region shorter than the sampling period: nearest samples
+                inside = sorted(samples, key=lambda x: min(abs(x[0] - lo), abs(x[0] - hi)))[:2]
+                where = "nearest to a timed region shorter than the 20 ms sampling period"
+        reasons = sorted(set().union(*(x[3] for x in inside)))
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": max(x[2] for x in samples),
+                "reasons": reasons, "samples": len(inside), "window": where}
 
 
 def traffic_per_launch():
@@ -226,11 +243,13 @@ def run_gpu(args):
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        t0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):
             layer_step(st, out, scratch)
         e1.record(stream)
         barrier()
+        clocks.mark(t0, time.time())
     step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     if not bool(torch.isfinite(out.float()).all()):
         raise RuntimeError("non-finite attention output")
@@ -530,7 +549,9 @@ def run_rotate_store(args):
                              st["layout"])
 
     with ClockSampler(0) as clocks:
+        t0 = time.time()
         ms = _timed_each(step, args.steps, args.warmup, device, flush)
+        clocks.mark(t0, time.time())
     live = int((st["slots"] >= 0).sum())
     read_bytes = 2 * n * H * D * 2 + n * 8 + 2 * D * D * 2
     write_bytes = 2 * live * H * 68
@@ -656,11 +677,13 @@ def run_mtp_verify(args):
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clocks:
+        t0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize(device)
+        clocks.mark(t0, time.time())
     ms = e0.elapsed_time(e1) / args.steps
     qrot = kernels.rotate(st["q"], st["rk"])
     for _ in range(3):
@@ -854,8 +877,8 @@ def profile_only(what):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="oscar", choices=["oscar", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
