@@ -1104,13 +1104,7 @@ static bool geo_ok(const oscar_geometry &g) {
 
 template <int MAXW, int NM>
 static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStream_t stream) {
-  static size_t configured = 0;
-  if (smem > configured) {
-    if (cudaFuncSetAttribute(history_attention_kernel<MAXW, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return OSCAR_ERR_LAUNCH;
-    configured = smem;
-  }
+  if (!ensure_dynamic_smem<history_attention_kernel<MAXW, NM>>(smem)) return OSCAR_ERR_LAUNCH;
   history_attention_kernel<MAXW, NM><<<grid, 32 * P.consumers, smem, stream>>>(P);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
@@ -1157,13 +1151,7 @@ static int sm_count() {
 }
 
 static int raw_launch(const RawParams &P, int32_t num_tasks, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(raw_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRawSmem) !=
-        cudaSuccess)
-      return OSCAR_ERR_LAUNCH;
-    configured = true;
-  }
+  if (!ensure_dynamic_smem<raw_attention_kernel>(kRawSmem)) return OSCAR_ERR_LAUNCH;
   dim3 grid(num_tasks, P.geo.kv_heads, P.ntiles);
   raw_attention_kernel<<<grid, 32 * kRawWarps, kRawSmem, stream>>>(P);
   OSCAR_CHECK_LAUNCH();
@@ -1332,12 +1320,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     rc = raw_launch(R, num_tasks, st);
     if (rc) return rc;
   }
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFinSmem) != cudaSuccess)
-      return OSCAR_ERR_LAUNCH;
-    configured = true;
-  }
+  if (!ensure_dynamic_smem<finalize_kernel>(kFinSmem)) return OSCAR_ERR_LAUNCH;
   FinalParams F{};
   F.partials = scratch_partials, F.lse = scratch_lse, F.split_slots = splits + 1, F.splits = splits;
   F.rows = n * hq, F.hq = hq, F.counts = counts;

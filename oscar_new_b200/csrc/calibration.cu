@@ -517,12 +517,7 @@ extern "C" int oscar_jacobi_rotations(const float *cov, int32_t batch, int32_t m
   if (batch == 0) return OSCAR_OK;
   if (!cov || !rotations || !eigenvalues || !info) return OSCAR_ERR_INVALID;
   const int smem = (int)sizeof(JacobiSmem);
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return OSCAR_ERR_LAUNCH;
-    configured = true;
-  }
+  if (!ensure_dynamic_smem<jacobi_kernel>(smem)) return OSCAR_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kJCtas * batch);
   cfg.blockDim = dim3(kJThreads);

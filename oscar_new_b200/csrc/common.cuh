@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/oscar_b200.h"
 
 #define OSCAR_DEVINL __device__ __forceinline__
@@ -233,6 +235,23 @@ OSCAR_DEVINL int window_index(int pos, const oscar_geometry &g) {
 }
 
 }  // namespace oscar
+
+// Opt kernel `Kernel` into `bytes` of dynamic shared memory on the current device.  The
+// attribute is per (kernel, device), so the grant is remembered per device; concurrent
+// first calls may both set it, which is harmless.
+template <auto Kernel>
+inline bool ensure_dynamic_smem(size_t bytes) {
+  static std::atomic<size_t> granted[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (granted[dev].load(std::memory_order_relaxed) >= bytes) return true;
+  if (cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return false;
+  size_t cur = granted[dev].load(std::memory_order_relaxed);
+  while (cur < bytes && !granted[dev].compare_exchange_weak(cur, bytes)) {
+  }
+  return true;
+}
 
 #define OSCAR_CHECK_LAUNCH()                                  \
   do {                                                        \

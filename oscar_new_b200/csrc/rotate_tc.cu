@@ -356,12 +356,7 @@ int launch_rotate_tc(const RotateParams &p, cudaStream_t stream) {
     total += t.tiles;
   }
   if (total == 0) return OSCAR_OK;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(rotate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc) != cudaSuccess)
-      return OSCAR_ERR_LAUNCH;
-    configured = true;
-  }
+  if (!ensure_dynamic_smem<rotate_tc_kernel>(kSmemTc)) return OSCAR_ERR_LAUNCH;
   rotate_tc_kernel<<<(unsigned)total, kThreads, kSmemTc, stream>>>(P);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;

@@ -86,20 +86,11 @@ static int launch_rotate(RotateParams p, cudaStream_t stream) {
     total += p.job[j].tiles;
   }
   const int smem = (rows * kDim + 2 * kBStageElems) * 2;
-  static bool configured[2] = {false, false};
   if (small) {
-    if (!configured[0]) {
-      if (cudaFuncSetAttribute(rotate_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return OSCAR_ERR_LAUNCH;
-      configured[0] = true;
-    }
+    if (!ensure_dynamic_smem<rotate_kernel<16>>(smem)) return OSCAR_ERR_LAUNCH;
     rotate_kernel<16><<<(unsigned)total, 128, smem, stream>>>(p);
   } else {
-    if (!configured[1]) {
-      if (cudaFuncSetAttribute(rotate_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return OSCAR_ERR_LAUNCH;
-      configured[1] = true;
-    }
+    if (!ensure_dynamic_smem<rotate_kernel<64>>(smem)) return OSCAR_ERR_LAUNCH;
     rotate_kernel<64><<<(unsigned)total, 256, smem, stream>>>(p);
   }
   OSCAR_CHECK_LAUNCH();
