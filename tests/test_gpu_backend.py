@@ -100,3 +100,32 @@ def test_impl_forward_replays_from_graph_captured_as_dummy(cuda_lib, oscar_env):
     expect, _ = sc.expected()
     assert rel_err(got, expect) < 1e-2, rel_err(got, expect)
     del graph
+
+
+def test_first_prefill_uses_flash_path_and_writes_the_same_cache(cuda_lib, oscar_env, monkeypatch):
+    """A batch whose host length bound equals its query lengths (no history yet) runs
+    the library flash-attention route; the same batch without the bound runs the
+    general path.  Outputs match the dense oracle; the caches are byte-identical."""
+    _, impl, _ = oscar_env
+    vc = fake_vllm_config(scheduler_config=SimpleNamespace(max_num_seqs=3, max_num_batched_tokens=2048),
+                          speculative_config=SimpleNamespace(num_speculative_tokens=3))
+    builder = OscarMetadataBuilder(SimpleNamespace(block_size=768, num_kv_heads=4), [LAYER], vc, torch.device(DEV))
+    results = []
+    for with_bound in (True, False):
+        sc = Scenario([300, 1100], [300, 1100], hq=24, h=4, cfg=make_config(4, 128, 3), seed=44, fill="none",
+                      rk=impl.rk.cpu(), rv=impl.rv.cpu())
+        cm = common_metadata(sc)
+        cm.query_start_loc_cpu = sc.plan.query_start_loc.clone()
+        cm.seq_lens_cpu_upper_bound = torch.tensor(sc.plan.seq_lens, dtype=torch.int32) if with_bound else None
+        meta = builder.build(0, cm)
+        assert meta.prefill_only == with_bound
+        q, k, v = sc.current()
+        n = q.shape[0]
+        out = torch.empty((n, 24 * 256), dtype=torch.bfloat16, device=DEV)
+        impl.forward(None, q.view(n, -1), k.view(n, -1), v.view(n, -1), sc.cache, meta, out)
+        got = out.view(n, 24, 256).float().cpu()
+        expect, _ = sc.expected()
+        assert rel_err(got, expect) < 1e-2, (with_bound, rel_err(got, expect))
+        torch.testing.assert_close(got, expect, atol=0.035, rtol=0.04)
+        results.append(sc.cache.view(-1).view(torch.uint8).cpu())
+    assert torch.equal(results[0], results[1])
