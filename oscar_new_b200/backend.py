@@ -146,12 +146,42 @@ class OscarAttentionImpl(AttentionImpl):
             raise ValueError("Attention output must be contiguous")
         if n == 0:
             return output
+        if getattr(meta, "prefill_only", False):
+            return self._first_prefill(query, key, value, meta, output)
         qrot = kernels.rotate_store(key, value, self.rk, self.rv, self.history, meta.slot_mapping, meta.counts,
                                     meta.layout, query=query)
         splits = decode_split_cap(meta.num_reqs, self.num_kv_heads, meta.max_query_len, n, self.num_heads)
         out = output.view(n, self.num_heads * self.head_size)
         kernels.decode_attention(qrot, query, key, value, self.history, self.window, meta, meta.layout,
                                  self.scale, splits, self.rv, out)
+        return output
+
+
+    def _first_prefill(self, query, key, value, meta, output):
+        """Requests that start at position 0: the cache gets the same INT2 history and
+        BF16 window writes as on the general path; attention is causal over the current
+        bf16 K/V only, computed by torch's flash-attention kernel (a library call, like
+        the reference's vendor fused attention for this case)."""
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        from . import kernels
+
+        kernels.rotate_store(key, value, self.rk, self.rv, self.history, meta.slot_mapping, meta.counts,
+                             meta.layout)
+        out = output.view(-1, self.num_heads, self.head_size)
+        starts = meta.query_start_loc_cpu.tolist()
+        with sdpa_kernel([SDPBackend.FLASH_ATTENTION]):
+            for i in range(meta.num_reqs):
+                a, b = starts[i], starts[i + 1]
+                if b == a:
+                    continue
+                o = F.scaled_dot_product_attention(query[a:b].transpose(0, 1).unsqueeze(0),
+                                                   key[a:b].transpose(0, 1).unsqueeze(0),
+                                                   value[a:b].transpose(0, 1).unsqueeze(0), is_causal=True,
+                                                   enable_gqa=True, scale=self.scale)
+                out[a:b].copy_(o[0].transpose(0, 1))
+        kernels.store_windows(key, value, self.window, meta, meta.layout)
         return output
 
 

@@ -54,6 +54,12 @@ class OscarMetadata:
     is_dummy: bool = False
     tasks: torch.Tensor | None = None
     task_count: torch.Tensor | None = None
+    # host-known first prefill: every request starts at position 0 (no history, no
+    # window yet); the forward then uses a library flash-attention kernel for the
+    # causal current-token attention (the reference hands this case to the vendor's
+    # fused attention, backend.py:175-193)
+    prefill_only: bool = False
+    query_start_loc_cpu: torch.Tensor | None = None
 
 
 class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
@@ -129,9 +135,18 @@ class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
 
         prepare_tasks(self.qstarts, self.counts, self.tasks, self.task_count, self.max_reqs, self.query_tile,
                       source_table=cm.block_table_tensor, table=self.table, copy_columns=copy_columns)
+        prefill_only, qcpu = False, None
+        bound = getattr(cm, "seq_lens_cpu_upper_bound", None)
+        qcpu_src = getattr(cm, "query_start_loc_cpu", None)
+        if not dummy and bound is not None and qcpu_src is not None and nr > 0 and cm.max_query_len > 16:
+            # the bound is exact for prefill rows and never below the true length, so
+            # bound == query length proves a zero-length prefix
+            qcpu = qcpu_src[: nr + 1].to(torch.int64)
+            prefill_only = bool(torch.equal(bound[:nr].to(torch.int64), qcpu[1:] - qcpu[:-1]))
         return OscarMetadata(self.qstarts, self.seqs, self.table, self.slots, self.counts, nr, nt,
                              cm.max_query_len, self.max_reqs, self.layout, is_dummy=dummy, tasks=self.tasks,
-                             task_count=self.task_count)
+                             task_count=self.task_count, prefill_only=prefill_only,
+                             query_start_loc_cpu=qcpu if prefill_only else None)
 
     def build_for_cudagraph_capture(self, common_attn_metadata):
         with dummy_run_scope(capturing=True):
