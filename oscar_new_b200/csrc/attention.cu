@@ -21,71 +21,15 @@
 // bytes of a token vector; the query fragment uses the same permutation.
 // MMAs use the swapped orientation (tokens / dims as M = 16, query rows as N = 8).
 #include <algorithm>
+#include <cstdlib>
 
-#include "common.cuh"
+#include "history_common.cuh"
 #include "rowgemm.cuh"
 
 namespace oscar {
 
 constexpr int kStages = 4;
 constexpr int kMaxConsumerWarps = 8;  // wider CTAs spill the O accumulator
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kTwo24 = 16777216.0f;
-constexpr float kRescaleSlack = 3.0f;  // lazily re-base the running max (p <= 2^3)
-
-struct HistParams {
-  const __nv_bfloat16 *query;  // rotated query rows, unit inner stride
-  int64_t qs0, qs1;
-  const uint8_t *history;
-  const int32_t *qstarts, *seq_lens, *table, *counts, *tasks, *task_count;
-  int32_t num_tasks;
-  float *partials;  // [n, Hq, split_slots, 256]
-  float *lse;       // [n, Hq, split_slots]
-  int32_t split_slots;
-  int32_t splits;
-  oscar_geometry geo;
-  float scale_log2;
-  // launch shape
-  int32_t heads_per_cta;  // HPC
-  int32_t ntiles;         // 8-row n-tiles per head
-  int32_t units;          // HPC * ntiles
-  int32_t warps_per_unit; // R_tok
-  int32_t consumers;      // units * warps_per_unit
-  int32_t chunk_tokens;   // CT
-  int32_t stage_bytes;
-  int32_t *status;        // nullable error word
-  // balanced splits (decode path): a request of L history tokens uses
-  // clamp(ceil(L / span), 1, splits) splits, span = max(kMinSplitTokens,
-  // total history * head groups / target_ctas); empty splits write only lse = -inf
-  int32_t balanced;
-  int32_t target_ctas;
-};
-
-constexpr int kMinSplitTokens = 1024;
-
-struct TaskInfo {
-  bool live;
-  int req, qoff, qstart, qlen, prefix, sink_len, recent_begin;
-};
-
-OSCAR_DEVINL TaskInfo load_task(int task, const int32_t *tasks, const int32_t *task_count,
-                                const int32_t *qstarts, const int32_t *seq_lens, const int32_t *counts,
-                                const oscar_geometry &g) {
-  TaskInfo ti{};
-  ti.live = task < task_count[0];
-  if (!ti.live) return ti;
-  ti.req = tasks[2 * task];
-  ti.qoff = tasks[2 * task + 1];
-  ti.qstart = qstarts[ti.req];
-  const int qend = min(qstarts[ti.req + 1], counts[1]);
-  ti.qlen = qend - ti.qstart;
-  const int seq = seq_lens[ti.req];
-  ti.prefix = seq - ti.qlen;
-  ti.sink_len = min(g.sink, ti.prefix);
-  ti.recent_begin = max(ti.sink_len, ti.prefix - g.recent);
-  return ti;
-}
-
 // Query operands of one 8-row n-tile, in the permuted contraction order the key codes
 // are read in (lane t owns dims [64t, 64t+64)):
 //  * qf[js]: fp16 fragments of the exact code functional sum_d q_d c_d, k-step js = 4i+p
@@ -152,30 +96,6 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
   Q.qsum[1] = __shfl_sync(0xffffffffu, s, 8 * t + 4);
   Q.qscale[0] = __shfl_sync(0xffffffffu, scale, 8 * t);
   Q.qscale[1] = __shfl_sync(0xffffffffu, scale, 8 * t + 4);
-}
-
-// Per-token coefficients of q.k with k = bf16(c*s + z) (the reference rounds the
-// dequantised key to bf16):  q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
-// with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.  Since
-// sum(q c) = sum(q b0) + 2 sum(q b1), the kernel uses M = sum(q c) (exact fp16 MMA) and
-// the two low-precision int8 sums A = sum(q b0), C = sum(q b0 b1):
-//   q.k = v0*sum(q) + (d1 + a/2) M - (a/2) A + b C.
-struct KeyCoef {
-  float v0, d1, a, b;
-};
-
-OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
-  const float s = half_bits_to_float(sz & 0xffffu), z = half_bits_to_float(sz >> 16);
-  const float v0 = round_bf16(z);
-  const float v1 = round_bf16(__fadd_rn(s, z));
-  const float v2 = round_bf16(__fadd_rn(2.f * s, z));
-  const float v3 = round_bf16(__fadd_rn(3.f * s, z));
-  KeyCoef k;
-  k.v0 = v0;
-  k.d1 = v1 - v0;
-  k.a = (v2 - v1) - (v1 - v0);
-  k.b = (v3 - v2) - (v1 - v0);
-  return k;
 }
 
 template <int MAXW, int NM>
@@ -1113,7 +1033,19 @@ static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStrea
 // Launch shape: each consumer warp owns one (KV head, 8-row) unit and NM = 2
 // consecutive 16-token m-tiles of every chunk; a chunk is all heads of
 // 16 * NM * warps_per_unit tokens (at most one 128-token kernel block).
+static bool history_tc_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("OSCAR_HISTORY_TC");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) {
+  if (history_tc_enabled()) {
+    const int rc = history_tc_launch(P, num_tasks, stream);
+    if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
+  }
   const oscar_geometry &g = P.geo;
   const int rows = g.query_tile * g.group;
   P.ntiles = (rows + 7) / 8;

@@ -1,0 +1,97 @@
+// Definitions shared by the two INT2 history attention kernels (attention.cu:
+// mma.sync with register-built operands; history_tc.cu: tcgen05 with the key
+// operands in tensor memory): launch parameters, task decoding (reference
+// oscar_ascend/kernels.py:290-330) and the per-token coefficients of the
+// bf16-rounded key.
+#pragma once
+
+#include "common.cuh"
+
+namespace oscar {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kTwo24 = 16777216.0f;
+constexpr float kRescaleSlack = 3.0f;  // lazily re-base the running max (p <= 2^3)
+
+struct HistParams {
+  const __nv_bfloat16 *query;  // rotated query rows, unit inner stride
+  int64_t qs0, qs1;
+  const uint8_t *history;
+  const int32_t *qstarts, *seq_lens, *table, *counts, *tasks, *task_count;
+  int32_t num_tasks;
+  float *partials;  // [n, Hq, split_slots, 256]
+  float *lse;       // [n, Hq, split_slots]
+  int32_t split_slots;
+  int32_t splits;
+  oscar_geometry geo;
+  float scale_log2;
+  // launch shape
+  int32_t heads_per_cta;  // HPC
+  int32_t ntiles;         // 8-row n-tiles per head
+  int32_t units;          // HPC * ntiles
+  int32_t warps_per_unit; // R_tok
+  int32_t consumers;      // units * warps_per_unit
+  int32_t chunk_tokens;   // CT
+  int32_t stage_bytes;
+  int32_t *status;        // nullable error word
+  // balanced splits (decode path): a request of L history tokens uses
+  // clamp(ceil(L / span), 1, splits) splits, span = max(kMinSplitTokens,
+  // total history * head groups / target_ctas); empty splits write only lse = -inf
+  int32_t balanced;
+  int32_t target_ctas;
+};
+
+constexpr int kMinSplitTokens = 1024;
+
+struct TaskInfo {
+  bool live;
+  int req, qoff, qstart, qlen, prefix, sink_len, recent_begin;
+};
+
+OSCAR_DEVINL TaskInfo load_task(int task, const int32_t *tasks, const int32_t *task_count,
+                                const int32_t *qstarts, const int32_t *seq_lens, const int32_t *counts,
+                                const oscar_geometry &g) {
+  TaskInfo ti{};
+  ti.live = task < task_count[0];
+  if (!ti.live) return ti;
+  ti.req = tasks[2 * task];
+  ti.qoff = tasks[2 * task + 1];
+  ti.qstart = qstarts[ti.req];
+  const int qend = min(qstarts[ti.req + 1], counts[1]);
+  ti.qlen = qend - ti.qstart;
+  const int seq = seq_lens[ti.req];
+  ti.prefix = seq - ti.qlen;
+  ti.sink_len = min(g.sink, ti.prefix);
+  ti.recent_begin = max(ti.sink_len, ti.prefix - g.recent);
+  return ti;
+}
+
+// Per-token coefficients of q.k with k = bf16(c*s + z) (the reference rounds the
+// dequantised key to bf16):  q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
+// with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.  Since
+// sum(q c) = sum(q b0) + 2 sum(q b1), the kernel uses M = sum(q c) (exact fp16 MMA) and
+// the two low-precision int8 sums A = sum(q b0), C = sum(q b0 b1):
+//   q.k = v0*sum(q) + (d1 + a/2) M - (a/2) A + b C.
+struct KeyCoef {
+  float v0, d1, a, b;
+};
+
+OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
+  const float s = half_bits_to_float(sz & 0xffffu), z = half_bits_to_float(sz >> 16);
+  const float v0 = round_bf16(z);
+  const float v1 = round_bf16(__fadd_rn(s, z));
+  const float v2 = round_bf16(__fadd_rn(2.f * s, z));
+  const float v3 = round_bf16(__fadd_rn(3.f * s, z));
+  KeyCoef k;
+  k.v0 = v0;
+  k.d1 = v1 - v0;
+  k.a = (v2 - v1) - (v1 - v0);
+  k.b = (v3 - v2) - (v1 - v0);
+  return k;
+}
+
+// tcgen05 history kernel (history_tc.cu); OSCAR_ERR_UNSUPPORTED for geometries it does
+// not cover (more than 32 query rows per KV head, other slot sizes).
+int history_tc_launch(const HistParams &P, int32_t num_tasks, cudaStream_t stream);
+
+}  // namespace oscar
