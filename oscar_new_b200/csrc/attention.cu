@@ -8,17 +8,19 @@
 // mbarrier completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast),
 // between its own chunks.  The 8 warps own (KV head, 8 query rows) units and 16-token
 // m-tiles; with no separate producer warp each thread may hold up to 255 registers,
-// which keeps four independent accumulators per code sum.
+// which keeps four independent key accumulators per m-tile.
 //
-// Dequantisation is factored out of the MMA: k = c*s + z per token, so
-//   q.k   = s * (q.c) + z * sum(q)          and   sum_t p_t v_t = sum_t (p_t s_t) c_t + sum_t p_t z_t.
-// Only the 2-bit codes enter the tensor cores, as fp16 subnormals: a single AND of
-// a packed 32-bit code word with 0x00030003 << 2p leaves two codes at bit 2p of each
-// half, i.e. the fp16 values c * 4^p * 2^-24, exactly.  The query is pre-divided by
-// 4^p (and the output multiplied back), so one LOP3 turns 4 codes of a word into
-// MMA operand halves with no conversion arithmetic.  The contraction dimension is
-// permuted (a bijection over the 256 dims) so that each lane reads only its own 16
-// bytes of a token vector; the query fragment uses the same permutation.
+// Keys: the reference rounds the dequantised key to bf16, so a token's 256 key
+// elements take only its four levels v_c = bf16(c*s + z).  Each token gets an 8-byte
+// table of those levels in fp16 (scaled by a power of two, which keeps them exact);
+// one PRMT whose selector nibbles come from one IMAD of two codes turns them into an
+// fp16 MMA operand register, and m16n8k16 MMAs against the (also power-of-two scaled,
+// exact) fp16 query give q.k_bf16 in fp32.  Values: sum_t p_t v_t =
+// sum_t (p_t s_t) c_t + sum_t p_t z_t; the 2-bit codes enter the fp16 MMA as
+// subnormals: one AND of a packed word with 0x00030003 << 2p leaves the fp16 values
+// c * 4^p * 2^-24 exactly, and the output is multiplied back by 4^p.  The contraction
+// dimension is permuted (a bijection over the 256 dims) so that each lane reads only
+// its own 16 bytes of a token vector; the query fragments use the same permutation.
 // MMAs use the swapped orientation (tokens / dims as M = 16, query rows as N = 8).
 #include <algorithm>
 #include <cstdlib>
@@ -30,22 +32,18 @@ namespace oscar {
 
 constexpr int kStages = 4;
 constexpr int kMaxConsumerWarps = 8;  // wider CTAs spill the O accumulator
-// Query operands of one 8-row n-tile, in the permuted contraction order the key codes
-// are read in (lane t owns dims [64t, 64t+64)):
-//  * qf[js]: fp16 fragments of the exact code functional sum_d q_d c_d, k-step js = 4i+p
-//    covering dims 16(4t+i) + {p, 8+p | 4+p, 12+p}, pre-divided by 4^p;
-//  * qb[j]:  int8 fragments (per-row scale) of the bit functionals, k32-step j = 2p+pr
-//    covering position p of words 4t + 2pr (first register) and 4t + 2pr + 1 (second),
-//    i.e. dims 16(4t+2pr) + 4b + p and 16(4t+2pr+1) + 4b + p, b = 0..3;
-//  * qsum / qscale of the rows 2t, 2t+1 this lane accumulates.
+// Query operands of one 8-row n-tile for the fp16 key MMAs, in the contraction order
+// the key tables are read in (lane t owns dims [64t, 64t+64); k16-step j = 4w + p covers
+// dims 16(4t+w) + {p, 4+p} in the first register and 16(4t+w) + {8+p, 12+p} in the
+// second):
+//  * qf: q * 2^e in fp16 (row max scaled into [2^14, 2^15)), exact for bf16 queries;
+//  * qm: 2^-e * log2(e) * softmax scale of the rows 2t, 2t+1 this lane accumulates.
 struct QueryFrags {
   uint32_t qf[16][2];
-  uint32_t qb[8][2];
-  float qsum[2];
-  float qscale[2];
+  float qm[2];
 };
 
-OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, bool valid) {
+OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, bool valid, float scale_log2) {
   const int lane = threadIdx.x & 31, t = lane & 3;
   uint32_t w[32];
 #pragma unroll
@@ -57,45 +55,27 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
     const uint32_t word = w[d >> 1];
     return bf16_bits_to_float((d & 1) ? (word >> 16) : (word & 0xffffu));
   };
-  float s = 0.f, amax = 0.f;
+  float amax = 0.f;
 #pragma unroll
-  for (int d = 0; d < 64; ++d) {
-    s += dim(d);
-    amax = fmaxf(amax, fabsf(dim(d)));
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float mul = 1.0f / (float)(1 << (2 * p));
-      Q.qf[4 * i + p][0] = pack_half2(dim(16 * i + p) * mul, dim(16 * i + 8 + p) * mul);
-      Q.qf[4 * i + p][1] = pack_half2(dim(16 * i + 4 + p) * mul, dim(16 * i + 12 + p) * mul);
-    }
-  s += __shfl_xor_sync(0xffffffffu, s, 1);
-  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  for (int d = 0; d < 64; ++d) amax = fmaxf(amax, fabsf(dim(d)));
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  const float scale = amax / 127.0f;
-  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-  auto q8 = [&](int d) { return (uint32_t)(min(max(__float2int_rn(dim(d) * inv), -127), 127) & 0xff); };
+  const uint32_t ex = (__float_as_uint(amax) >> 23) & 0xffu;
+  const uint32_t exc = ex < 16u ? 16u : ex;
+  const bool any = amax > 0.f;
+  const float up = any ? __uint_as_float((268u - exc) << 23) : 0.f;
+  const float down = any ? __uint_as_float((exc - 14u) << 23) * scale_log2 : 0.f;
 #pragma unroll
-  for (int p = 0; p < 4; ++p)
+  for (int wd = 0; wd < 4; ++wd)
 #pragma unroll
-    for (int pr = 0; pr < 2; ++pr) {
-      uint32_t r0 = 0, r1 = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        r0 |= q8(16 * (2 * pr) + 4 * b + p) << (8 * b);
-        r1 |= q8(16 * (2 * pr + 1) + 4 * b + p) << (8 * b);
-      }
-      Q.qb[2 * p + pr][0] = r0;
-      Q.qb[2 * p + pr][1] = r1;
+    for (int p = 0; p < 4; ++p) {
+      const int d = 16 * wd + p;
+      Q.qf[4 * wd + p][0] = pack_half2(dim(d) * up, dim(d + 4) * up);
+      Q.qf[4 * wd + p][1] = pack_half2(dim(d + 8) * up, dim(d + 12) * up);
     }
-  // s / scale are row-gi values on all four t lanes; the S fragment needs rows 2t, 2t+1.
-  Q.qsum[0] = __shfl_sync(0xffffffffu, s, 8 * t);
-  Q.qsum[1] = __shfl_sync(0xffffffffu, s, 8 * t + 4);
-  Q.qscale[0] = __shfl_sync(0xffffffffu, scale, 8 * t);
-  Q.qscale[1] = __shfl_sync(0xffffffffu, scale, 8 * t + 4);
+  // down is a row-gi value on all four t lanes; the S fragment needs rows 2t, 2t+1.
+  Q.qm[0] = __shfl_sync(0xffffffffu, down, 8 * t);
+  Q.qm[1] = __shfl_sync(0xffffffffu, down, 8 * t + 4);
 }
 
 template <int MAXW, int NM>
@@ -209,13 +189,12 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
   const int qtok = ti.qstart + ti.qoff + r_mine / g.group;
   const int qhead = head * g.group + r_mine % g.group;
   QueryFrags Q;
-  load_query_frags(Q, P.query + (int64_t)qtok * P.qs0 + (int64_t)qhead * P.qs1, rvalid);
+  load_query_frags(Q, P.query + (int64_t)qtok * P.qs0 + (int64_t)qhead * P.qs1, rvalid, P.scale_log2);
 
   float o[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f}, zp_run[2] = {0.f, 0.f};
-  const float sl2 = P.scale_log2;
   bool ok = true;
 
 #pragma unroll 1
@@ -249,90 +228,57 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
         va[j] = tpos + gi >= lo && tpos + gi < hi;
         vb[j] = tpos + gi + 8 >= lo && tpos + gi + 8 < hi;
       }
-      // ---- S^T (tokens x rows): exact sum q c on fp16, bit sums on int8 ----
+      // ---- S^T (tokens x rows) on fp16 tensor cores.  Each 2-bit key code becomes its
+      // bf16 level (exact in fp16 after the token's power-of-two scale) through the
+      // token's byte table: one PRMT turns two codes into an MMA operand register. ----
       uint32_t kaw[NM][4], kbw[NM][4];
+      KeyLut lA[NM], lB[NM];
+      uint32_t vsz[NM][2];
 #pragma unroll
       for (int j = 0; j < NM; ++j) {
-        const uint4 ka = *reinterpret_cast<const uint4 *>(tl[j] + gi * token_bytes + 16 * t);
-        const uint4 kb = *reinterpret_cast<const uint4 *>(tl[j] + (gi + 8) * token_bytes + 16 * t);
+        const uint8_t *ra = tl[j] + gi * token_bytes, *rb = ra + 8 * token_bytes;
+        const uint4 ka = *reinterpret_cast<const uint4 *>(ra + 16 * t);
+        const uint4 kb = *reinterpret_cast<const uint4 *>(rb + 16 * t);
         kaw[j][0] = ka.x, kaw[j][1] = ka.y, kaw[j][2] = ka.z, kaw[j][3] = ka.w;
         kbw[j][0] = kb.x, kbw[j][1] = kb.y, kbw[j][2] = kb.z, kbw[j][3] = kb.w;
+        lA[j] = key_lut(*reinterpret_cast<const uint32_t *>(ra + 64));
+        lB[j] = key_lut(*reinterpret_cast<const uint32_t *>(rb + 64));
+        vsz[j][0] = *reinterpret_cast<const uint32_t *>(ra + g.vector_bytes + 64);
+        vsz[j][1] = *reinterpret_cast<const uint32_t *>(rb + g.vector_bytes + 64);
       }
-      float sc[NM][4][4];  // [m-tile][bit position p][fragment]: four independent HMMA chains
+      float sc[NM][2][4];  // [m-tile][chain (even / odd code position)][fragment]
 #pragma unroll
       for (int j = 0; j < NM; ++j)
 #pragma unroll
-        for (int p = 0; p < 4; ++p)
+        for (int u = 0; u < 2; ++u)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) sc[j][p][e] = 0.f;
+          for (int e = 0; e < 4; ++e) sc[j][u][e] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int wd = 0; wd < 4; ++wd) {
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const uint32_t msk = 0x00030003u << (2 * p);
 #pragma unroll
           for (int j = 0; j < NM; ++j) {
-            mma_f16_16816(sc[j][p], kaw[j][i] & msk, kbw[j][i] & msk, (kaw[j][i] >> 8) & msk, (kbw[j][i] >> 8) & msk,
-                          Q.qf[4 * i + p][0], Q.qf[4 * i + p][1]);
-          }
-        }
-      }
-      // A = sum q b0 and C = sum q b0 b1.  Operands are single masks of the packed word
-      // (u8 values 4^p); positions are accumulated from p = 3 down with an exact >> 2
-      // between groups, which leaves sum_p (.)_p at unit weight.
-      uint32_t kay[NM][4], kby[NM][4];
-      int acc_a[NM][4], acc_c[NM][4];
-#pragma unroll
-      for (int j = 0; j < NM; ++j) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          kay[j][i] = kaw[j][i] & (kaw[j][i] >> 1);
-          kby[j][i] = kbw[j][i] & (kbw[j][i] >> 1);
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc_a[j][e] = acc_c[j][e] = 0;
-      }
-#pragma unroll
-      for (int p = 3; p >= 0; --p) {
-        if (p < 3) {
-#pragma unroll
-          for (int j = 0; j < NM; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc_a[j][e] >>= 2, acc_c[j][e] >>= 2;
-        }
-        const uint32_t m = 0x01010101u << (2 * p);
-#pragma unroll
-        for (int pr = 0; pr < 2; ++pr) {
-          const int w0 = 2 * pr, w1 = 2 * pr + 1;
-#pragma unroll
-          for (int j = 0; j < NM; ++j) {
-            mma_u8s8_16832(acc_a[j], kaw[j][w0] & m, kbw[j][w0] & m, kaw[j][w1] & m, kbw[j][w1] & m,
-                           Q.qb[2 * p + pr][0], Q.qb[2 * p + pr][1]);
-            mma_u8s8_16832(acc_c[j], kay[j][w0] & m, kby[j][w0] & m, kay[j][w1] & m, kby[j][w1] & m,
-                           Q.qb[2 * p + pr][0], Q.qb[2 * p + pr][1]);
+            // codes of position p of the four bytes, in bits 0-1 of each byte
+            const uint32_t xa = (kaw[j][wd] >> (2 * p)) & 0x03030303u;
+            const uint32_t xb = (kbw[j][wd] >> (2 * p)) & 0x03030303u;
+            const uint32_t a0 = prmt(lA[j].lo, lA[j].hi, lut_sel_lo(xa));
+            const uint32_t a1 = prmt(lB[j].lo, lB[j].hi, lut_sel_lo(xb));
+            const uint32_t a2 = prmt(lA[j].lo, lA[j].hi, lut_sel_lo(xa >> 16));
+            const uint32_t a3 = prmt(lB[j].lo, lB[j].hi, lut_sel_lo(xb >> 16));
+            mma_f16_16816(sc[j][p & 1], a0, a1, a2, a3, Q.qf[4 * wd + p][0], Q.qf[4 * wd + p][1]);
           }
         }
       }
       // ---- logits (log2 domain) ----
       float lg[NM][4];
-      uint32_t vsz[NM][2];
 #pragma unroll
       for (int j = 0; j < NM; ++j) {
-        const uint32_t kszA = *reinterpret_cast<const uint32_t *>(tl[j] + gi * token_bytes + 64);
-        const uint32_t kszB = *reinterpret_cast<const uint32_t *>(tl[j] + (gi + 8) * token_bytes + 64);
-        vsz[j][0] = *reinterpret_cast<const uint32_t *>(tl[j] + gi * token_bytes + g.vector_bytes + 64);
-        vsz[j][1] = *reinterpret_cast<const uint32_t *>(tl[j] + (gi + 8) * token_bytes + g.vector_bytes + 64);
-        const KeyCoef ka = key_coefficients(kszA), kb = key_coefficients(kszB);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const KeyCoef &kc = e < 2 ? ka : kb;
-          const int r = e & 1;
-          const float ha = 0.5f * kc.a;
-          float dot = kc.v0 * Q.qsum[r];
-          dot = fmaf((kc.d1 + ha) * kTwo24, (sc[j][0][e] + sc[j][1][e]) + (sc[j][2][e] + sc[j][3][e]), dot);
-          dot = fmaf(-ha * Q.qscale[r], (float)acc_a[j][e], dot);
-          dot = fmaf(kc.b * Q.qscale[r], (float)acc_c[j][e], dot);
-          lg[j][e] = ((e < 2) ? va[j] : vb[j]) ? dot * sl2 : -INFINITY;
+          const float dot = sc[j][0][e] + sc[j][1][e];
+          const float mul = (e < 2 ? lA[j].inv : lB[j].inv) * Q.qm[e & 1];
+          lg[j][e] = ((e < 2) ? va[j] : vb[j]) ? dot * mul : -INFINITY;
         }
       }
       // ---- online softmax over the warp's 16*NM tokens, lazy re-basing ----

@@ -90,6 +90,38 @@ OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
   return k;
 }
 
+// The four bf16 key levels v_c = bf16(c*s + z) of one token as an fp16 byte table for
+// PRMT: levels scaled by 2^e (max |v| in [2^14, 2^15)), which fp16 holds exactly (a
+// level smaller than 2^-31 max |v| may lose low bits).  lo = low bytes of the four
+// halves, hi = high bytes, so selector nibbles (c, 4 + c) fetch level c.  inv = 2^-e.
+struct KeyLut {
+  uint32_t lo, hi;
+  float inv;
+};
+
+OSCAR_DEVINL KeyLut key_lut(uint32_t sz) {
+  const float s = half_bits_to_float(sz & 0xffffu), z = half_bits_to_float(sz >> 16);
+  const float v0 = round_bf16(z);
+  const float v1 = round_bf16(__fadd_rn(s, z));
+  const float v2 = round_bf16(__fadd_rn(2.f * s, z));
+  const float v3 = round_bf16(__fadd_rn(3.f * s, z));
+  // s >= 2^-14 for every written slot, so the levels increase and max |v| is at an end
+  const uint32_t ex = (__float_as_uint(fmaxf(fabsf(v0), fabsf(v3))) >> 23) & 0xffu;
+  const uint32_t exc = ex < 16u ? 16u : ex;  // unwritten slots (masked later) stay finite
+  // 2^(141 - ex) scales [2^(ex-127), 2^(ex-126)) to [2^14, 2^15)
+  const float up = __uint_as_float((268u - exc) << 23);
+  const uint32_t h01 = pack_half2(v0 * up, v1 * up), h23 = pack_half2(v2 * up, v3 * up);
+  KeyLut k;
+  k.lo = prmt(h01, h23, 0x6420u);
+  k.hi = prmt(h01, h23, 0x7531u);
+  k.inv = __uint_as_float((exc - 14u) << 23);
+  return k;
+}
+
+// PRMT selector of the two codes in bits 0-1 of bytes 0 and 1 of x (one IMAD): nibbles
+// (c0, 4 + c0, c1, 4 + c1) fetch the two fp16 levels from (lo, hi).
+OSCAR_DEVINL uint32_t lut_sel_lo(uint32_t x) { return x * 0x11u + 0x4040u; }
+
 // tcgen05 history kernel (history_tc.cu); OSCAR_ERR_UNSUPPORTED for geometries it does
 // not cover (more than 32 query rows per KV head, other slot sizes).
 int history_tc_launch(const HistParams &P, int32_t num_tasks, cudaStream_t stream);
