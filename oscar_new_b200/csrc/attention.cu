@@ -4,11 +4,11 @@
 //
 // History kernel (INT2, rotated space).  One CTA = one (task, split, head group).
 // Lane 0 of warp 0 streams chunks of the paged K stripe (at most one 128-token kernel
-// block) into a 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk,
+// block) into a 3- or 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk,
 // mbarrier completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast),
-// between its own chunks.  The 8 warps own (KV head, 8 query rows) units and 16-token
-// m-tiles; with no separate producer warp each thread may hold up to 255 registers,
-// which keeps four independent key accumulators per m-tile.
+// between its own chunks.  The warps own (KV head, 8 query rows) units and two 16-token
+// m-tiles each; with no separate producer warp.  Narrow launches (all KV heads x row
+// tiles in 4 warps) run 3 CTAs per SM at <= 168 registers, wider ones 8 warps per CTA.
 //
 // Keys: the reference rounds the dequantised key to bf16, so a token's 256 key
 // elements take only its four levels v_c = bf16(c*s + z).  Each token gets an 8-byte
@@ -30,8 +30,12 @@
 
 namespace oscar {
 
-constexpr int kStages = 4;
 constexpr int kMaxConsumerWarps = 8;  // wider CTAs spill the O accumulator
+// Narrow launch (every KV head x row tile of a task fits in 4 warps, e.g. decode with
+// 4 KV heads): 4-warp CTAs at <= 168 registers, 3 resident per SM (12 warps instead of
+// 8 hide more of the operand-building latency).
+constexpr int kNarrowWarps = 4;
+constexpr int kNarrowCtasPerSm = 3;
 // Query operands of one 8-row n-tile for the fp16 key MMAs, in the contraction order
 // the key tables are read in (lane t owns dims [64t, 64t+64); k16-step j = 4w + p covers
 // dims 16(4t+w) + {p, 4+p} in the first register and 16(4t+w) + {8+p, 12+p} in the
@@ -78,8 +82,8 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
   Q.qm[1] = __shfl_sync(0xffffffffu, down, 8 * t + 4);
 }
 
-template <int MAXW, int NM>
-__global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistParams P) {
+template <int MAXW, int NM, int STAGES, int MINB>
+__global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(HistParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   const oscar_geometry &g = P.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -129,10 +133,10 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
   const int nchunks = hi > lo ? (hi - 1) / CT - first_chunk + 1 : 0;
 
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-  uint64_t *empty = full + kStages;
+  uint64_t *empty = full + STAGES;
   uint8_t *stages = smem + 128;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], P.consumers);
     }
@@ -142,14 +146,14 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
 
   const int hpc = P.heads_per_cta;
   const int token_bytes = hpc * g.slot_bytes;
-  // Copies are issued by lane 0 of warp 0 between its own chunks: chunk c + kStages - 1
+  // Copies are issued by lane 0 of warp 0 between its own chunks: chunk c + STAGES - 1
   // as soon as the consumers have released its stage (non-blocking probe), and chunk c
   // at the latest before warp 0 needs it (bounded blocking wait).  Keeping the CTA at
   // 8 warps (2 per scheduler) leaves each thread up to 255 registers.
   const int32_t *trow = P.table + (int64_t)ti.req * g.table_stride;
   int issued = 0;
   auto issue_one = [&](int c) {
-    const int s = c % kStages;
+    const int s = c % STAGES;
     const int pos = (first_chunk + c) * CT;
     const int64_t slot0 = (int64_t)trow[pos / kKernelBlock] * kKernelBlock + pos % kKernelBlock;
     const uint8_t *src = P.history + (slot0 / g.block_tokens) * g.page_bytes +
@@ -166,12 +170,12 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
   // returns false when a bounded wait for a free stage gave up
   auto pump = [&](int c) -> bool {
     while (issued <= c && issued < nchunks) {
-      if (issued >= kStages && !mbar_wait_bounded(&empty[issued % kStages], ((issued / kStages) - 1) & 1))
+      if (issued >= STAGES && !mbar_wait_bounded(&empty[issued % STAGES], ((issued / STAGES) - 1) & 1))
         return false;
       issue_one(issued++);
     }
-    while (issued < nchunks && issued < c + kStages) {
-      if (issued >= kStages && !mbar_test(&empty[issued % kStages], ((issued / kStages) - 1) & 1)) break;
+    while (issued < nchunks && issued < c + STAGES) {
+      if (issued >= STAGES && !mbar_test(&empty[issued % STAGES], ((issued / STAGES) - 1) & 1)) break;
       issue_one(issued++);
     }
     return true;
@@ -199,7 +203,7 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
 
 #pragma unroll 1
   for (int c = 0; c < nchunks && ok; ++c) {
-    const int s = c % kStages;
+    const int s = c % STAGES;
     if (warp == 0) {
       bool pumped = true;
       if (lane == 0) pumped = pump(c);
@@ -209,7 +213,7 @@ __global__ void __launch_bounds__(32 * MAXW, 1) history_attention_kernel(HistPar
         break;
       }
     }
-    if (!mbar_wait_bounded(&full[s], (c / kStages) & 1)) {
+    if (!mbar_wait_bounded(&full[s], (c / STAGES) & 1)) {
       ok = false;
       if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
       break;
@@ -968,10 +972,10 @@ static bool geo_ok(const oscar_geometry &g) {
          g.recent >= 0 && g.query_tile > 0 && g.table_stride > 0;
 }
 
-template <int MAXW, int NM>
+template <int MAXW, int NM, int STAGES, int MINB>
 static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStream_t stream) {
-  if (!ensure_dynamic_smem<history_attention_kernel<MAXW, NM>>(smem)) return OSCAR_ERR_LAUNCH;
-  history_attention_kernel<MAXW, NM><<<grid, 32 * P.consumers, smem, stream>>>(P);
+  if (!ensure_dynamic_smem<history_attention_kernel<MAXW, NM, STAGES, MINB>>(smem)) return OSCAR_ERR_LAUNCH;
+  history_attention_kernel<MAXW, NM, STAGES, MINB><<<grid, 32 * P.consumers, smem, stream>>>(P);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
 }
@@ -979,6 +983,18 @@ static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStrea
 // Launch shape: each consumer warp owns one (KV head, 8-row) unit and NM = 2
 // consecutive 16-token m-tiles of every chunk; a chunk is all heads of
 // 16 * NM * warps_per_unit tokens (at most one 128-token kernel block).
+// SM count of the current device (cached per device).
+static int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    cache[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+  }
+  return cache[dev];
+}
+
 static bool history_tc_enabled() {
   static const bool on = [] {
     const char *v = getenv("OSCAR_HISTORY_TC");
@@ -996,36 +1012,30 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) 
   const int rows = g.query_tile * g.group;
   P.ntiles = (rows + 7) / 8;
   if (P.ntiles > kMaxConsumerWarps) return OSCAR_ERR_UNSUPPORTED;
+  constexpr int NM = 2;
+  const bool narrow = P.ntiles * g.kv_heads <= kNarrowWarps;
+  const int max_warps = narrow ? kNarrowWarps : kMaxConsumerWarps;
   int hpc = g.kv_heads;
-  while (hpc * P.ntiles > kMaxConsumerWarps) hpc = (hpc + 1) / 2;
+  while (hpc * P.ntiles > max_warps) hpc = (hpc + 1) / 2;
   if (g.kv_heads % hpc) hpc = 1;
   P.heads_per_cta = hpc;
   P.units = hpc * P.ntiles;
-  constexpr int NM = 2;
-  int wpu = P.units >= 8 ? 1 : 8 / P.units;
+  int wpu = P.units >= max_warps ? 1 : max_warps / P.units;
   while (wpu > 1 && 16 * NM * wpu > kKernelBlock) wpu >>= 1;
   P.warps_per_unit = wpu;
   P.consumers = P.units * wpu;
   P.chunk_tokens = 16 * NM * wpu;
   P.stage_bytes = P.chunk_tokens * hpc * g.slot_bytes;
+  const int stages = narrow ? 3 : 4;
   const size_t xch = ((size_t)(P.consumers - P.units) * (16 * 4 * 32 + 2 * 32) + (size_t)P.consumers * 4 * 32) * 4;
-  size_t smem = 128 + (size_t)kStages * P.stage_bytes;
+  size_t smem = 128 + (size_t)stages * P.stage_bytes;
   if (smem < 128 + xch) smem = 128 + xch;
   if (smem > 227 * 1024) return OSCAR_ERR_UNSUPPORTED;
   dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
-  return launch_history<kMaxConsumerWarps, NM>(P, grid, smem, stream);
-}
-
-// SM count of the current device (cached per device).
-static int sm_count() {
-  static int cache[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int v = 0;
-    cache[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+  if (narrow) {
+    return launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream);
   }
-  return cache[dev];
+  return launch_history<kMaxConsumerWarps, NM, 4, 1>(P, grid, smem, stream);
 }
 
 static int raw_launch(const RawParams &P, int32_t num_tasks, cudaStream_t stream) {
