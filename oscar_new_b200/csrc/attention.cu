@@ -6,9 +6,10 @@
 // Lane 0 of warp 0 streams chunks of the paged K stripe (at most one 128-token kernel
 // block) into a 3- or 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk,
 // mbarrier completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast),
-// between its own chunks.  The warps own (KV head, 8 query rows) units and two 16-token
-// m-tiles each; with no separate producer warp.  Narrow launches (all KV heads x row
-// tiles in 4 warps) run 3 CTAs per SM at <= 168 registers, wider ones 8 warps per CTA.
+// between its own chunks (there is no separate producer warp).  The warps own (KV head,
+// 8 query rows) units and two 16-token m-tiles each.  Narrow launches (all KV heads x
+// row tiles in 4 warps) run 3 CTAs per SM at <= 168 registers, wider ones 8 warps per
+// CTA at up to 255 registers.
 //
 // Keys: the reference rounds the dequantised key to bf16, so a token's 256 key
 // elements take only its four levels v_c = bf16(c*s + z).  Each token gets an 8-byte
