@@ -758,9 +758,12 @@ struct FinalParams {
   __nv_bfloat16 *out;
 };
 
-// 16-row tiles, 4 warps: one CTA per 16 output rows, so a decode step (n * Hq rows)
-// spreads over n * Hq / 16 CTAs.
+// 8 output rows per CTA on a 16-row GEMM tile (rows 8..15 of the tile are zero), 4 warps:
+// a decode step (n * Hq rows) spreads over n * Hq / 8 CTAs.  Each warp merges two rows
+// with the loads of both rows in flight together (the merge is latency-bound: a row
+// reads one 1 KB partial per used split).
 constexpr int kFinRows = 16;
+constexpr int kFinLive = 8;
 constexpr int kFinThreads = 128;
 constexpr int kFinSmem = (kFinRows * kDim + 2 * kBStageElems) * 2 + 2 * kFinRows * 4;
 
@@ -771,69 +774,92 @@ __global__ void __launch_bounds__(kFinThreads) finalize_kernel(FinalParams P) {
   float *s_la = reinterpret_cast<float *>(sB + 2 * kBStageElems);  // [16]
   float *s_lb = s_la + kFinRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t row0 = (int64_t)blockIdx.x * kFinRows;
+  const int64_t row0 = (int64_t)blockIdx.x * kFinLive;
   const int32_t active = P.counts[1];
-  for (int i = 0; i < kFinRows / 4; ++i) {
-    const int r = warp * (kFinRows / 4) + i;
-    const int64_t row = row0 + r;
-    const bool valid = row < P.rows && row / P.hq < active;
+  // zero tile rows 8..15 (16 bytes per thread)
+  for (int i = threadIdx.x; i < (kFinRows - kFinLive) * kDim / 8; i += kFinThreads)
+    reinterpret_cast<uint4 *>(sA + kFinLive * kDim)[i] = make_uint4(0, 0, 0, 0);
+  constexpr int RW = kFinLive / 4;  // rows per warp
+  float m[RW], w0[RW], w1[RW], den[RW];
+  bool valid[RW];
+#pragma unroll
+  for (int i = 0; i < RW; ++i) {
+    const int64_t row = row0 + warp * RW + i;
+    valid[i] = row < P.rows && row / P.hq < active;
     // lane s holds split s's lse (splits <= 64: two per lane); warp max / weights
     const float *lrow = P.lse + row * P.split_slots;
-    const float l0 = valid && lane < P.splits ? lrow[lane] : -INFINITY;
-    const float l1 = valid && lane + 32 < P.splits ? lrow[lane + 32] : -INFINITY;
-    float m = fmaxf(l0, l1);
+    const float l0 = valid[i] && lane < P.splits ? lrow[lane] : -INFINITY;
+    const float l1 = valid[i] && lane + 32 < P.splits ? lrow[lane + 32] : -INFINITY;
+    float mm = fmaxf(l0, l1);
 #pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float safe = m == -INFINITY ? 0.f : m;
-    const float w0 = expf(l0 - safe), w1 = expf(l1 - safe);
-    float den = w0 + w1;
+    for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    const float safe = mm == -INFINITY ? 0.f : mm;
+    w0[i] = expf(l0 - safe), w1[i] = expf(l1 - safe);
+    float d = w0[i] + w1[i];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    // four splits per group: all loads of the group are in flight before any is used
-    for (int s0 = 0; s0 < P.splits; s0 += 4) {
-      float w[4];
-      float4 x[4][2];
+    for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    m[i] = mm, den[i] = d;
+  }
+  float macc[RW][8];
+#pragma unroll
+  for (int i = 0; i < RW; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) macc[i][e] = 0.f;
+  // four splits of every row per group: all loads of the group are in flight before any is used
+  for (int s0 = 0; s0 < P.splits; s0 += 4) {
+    float w[RW][4];
+    float4 x[RW][4][2];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      const int64_t row = row0 + warp * RW + i;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int sp = s0 + u;
-        const float ws = __shfl_sync(0xffffffffu, sp < 32 ? w0 : w1, sp & 31);
-        w[u] = sp < P.splits ? ws : 0.f;
-        if (w[u] != 0.f) {
+        const float ws = __shfl_sync(0xffffffffu, sp < 32 ? w0[i] : w1[i], sp & 31);
+        w[i][u] = sp < P.splits ? ws : 0.f;
+        if (w[i][u] != 0.f) {
           const float4 *src = reinterpret_cast<const float4 *>(P.partials + (row * P.split_slots + sp) * kDim + lane * 8);
-          x[u][0] = src[0], x[u][1] = src[1];
+          x[i][u][0] = src[0], x[i][u][1] = src[1];
         } else {
-          x[u][0] = x[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          x[i][u][0] = x[i][u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
+    }
+#pragma unroll
+    for (int i = 0; i < RW; ++i)
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        acc[0] = fmaf(w[u], x[u][0].x, acc[0]), acc[1] = fmaf(w[u], x[u][0].y, acc[1]);
-        acc[2] = fmaf(w[u], x[u][0].z, acc[2]), acc[3] = fmaf(w[u], x[u][0].w, acc[3]);
-        acc[4] = fmaf(w[u], x[u][1].x, acc[4]), acc[5] = fmaf(w[u], x[u][1].y, acc[5]);
-        acc[6] = fmaf(w[u], x[u][1].z, acc[6]), acc[7] = fmaf(w[u], x[u][1].w, acc[7]);
+        const float wu = w[i][u];
+        macc[i][0] = fmaf(wu, x[i][u][0].x, macc[i][0]), macc[i][1] = fmaf(wu, x[i][u][0].y, macc[i][1]);
+        macc[i][2] = fmaf(wu, x[i][u][0].z, macc[i][2]), macc[i][3] = fmaf(wu, x[i][u][0].w, macc[i][3]);
+        macc[i][4] = fmaf(wu, x[i][u][1].x, macc[i][4]), macc[i][5] = fmaf(wu, x[i][u][1].y, macc[i][5]);
+        macc[i][6] = fmaf(wu, x[i][u][1].z, macc[i][6]), macc[i][7] = fmaf(wu, x[i][u][1].w, macc[i][7]);
       }
-    }
-    const float inv = 1.0f / fmaxf(den, 1e-30f);
+  }
+#pragma unroll
+  for (int i = 0; i < RW; ++i) {
+    const int r = warp * RW + i;
+    const int64_t row = row0 + r;
+    const float inv = 1.0f / fmaxf(den[i], 1e-30f);
     uint4 o;
-    o.x = pack_bf162(acc[0] * inv, acc[1] * inv);
-    o.y = pack_bf162(acc[2] * inv, acc[3] * inv);
-    o.z = pack_bf162(acc[4] * inv, acc[5] * inv);
-    o.w = pack_bf162(acc[6] * inv, acc[7] * inv);
+    o.x = pack_bf162(macc[i][0] * inv, macc[i][1] * inv);
+    o.y = pack_bf162(macc[i][2] * inv, macc[i][3] * inv);
+    o.z = pack_bf162(macc[i][4] * inv, macc[i][5] * inv);
+    o.w = pack_bf162(macc[i][6] * inv, macc[i][7] * inv);
     *reinterpret_cast<uint4 *>(sA + r * kDim + ((lane ^ (r & 7)) << 3)) = o;
     if (lane == 0) {
-      s_la[r] = den > 0.f ? m + logf(fmaxf(den, 1e-30f)) : -INFINITY;
-      s_lb[r] = valid ? P.lse[row * P.split_slots + P.splits] : -INFINITY;
+      s_la[r] = den[i] > 0.f ? m[i] + logf(fmaxf(den[i], 1e-30f)) : -INFINITY;
+      s_lb[r] = valid[i] ? P.lse[row * P.split_slots + P.splits] : -INFINITY;
     }
   }
   float acc[1][8][4];
   rowgemm_mainloop<1, kFinThreads>(acc, sA, sB, BMatrix{P.rv, 1, 256});  // B(k, n) = Rv[n][k]
   const int wn = warp & 3, gq = lane >> 2, t = lane & 3;
-#pragma unroll
-  for (int hb = 0; hb < 2; ++hb) {
-    const int r = gq + 8 * hb;
+  {
+    const int hb = 0;  // tile rows 0..7 are this CTA's rows
+    const int r = gq;
     const int64_t row = row0 + r;
-    if (row >= P.rows) continue;
+    if (row >= P.rows) return;
     const float xa = s_la[r], xb = s_lb[r];
     float m = fmaxf(xa, xb);
     m = m == -INFINITY ? 0.f : m;
@@ -1215,7 +1241,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
   F.rows = n * hq, F.hq = hq, F.counts = counts;
   F.rv = reinterpret_cast<const __nv_bfloat16 *>(rv);
   F.out = reinterpret_cast<__nv_bfloat16 *>(output);
-  finalize_kernel<<<(unsigned)((F.rows + kFinRows - 1) / kFinRows), kFinThreads, kFinSmem, st>>>(F);
+  finalize_kernel<<<(unsigned)((F.rows + kFinLive - 1) / kFinLive), kFinThreads, kFinSmem, st>>>(F);
   OSCAR_CHECK_LAUNCH();
   if (window_programs > 0) {
     window_store_kernel<<<window_programs, 256, 0, st>>>(
