@@ -264,13 +264,15 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
         for (int p = 0; p < 4; ++p) {
 #pragma unroll
           for (int j = 0; j < NM; ++j) {
-            // codes of position p of the four bytes, in bits 0-1 of each byte
+            // codes of position p of the four bytes, in bits 0-1 of each byte; one IMAD
+            // gives the PRMT selectors of bytes (0, 1) in its low and (2, 3) in its high half
             const uint32_t xa = (kaw[j][wd] >> (2 * p)) & 0x03030303u;
             const uint32_t xb = (kbw[j][wd] >> (2 * p)) & 0x03030303u;
-            const uint32_t a0 = prmt(lA[j].lo, lA[j].hi, lut_sel_lo(xa));
-            const uint32_t a1 = prmt(lB[j].lo, lB[j].hi, lut_sel_lo(xb));
-            const uint32_t a2 = prmt(lA[j].lo, lA[j].hi, lut_sel_lo(xa >> 16));
-            const uint32_t a3 = prmt(lB[j].lo, lB[j].hi, lut_sel_lo(xb >> 16));
+            const uint32_t sa = xa * 0x11u + 0x40404040u, sb = xb * 0x11u + 0x40404040u;
+            const uint32_t a0 = prmt(lA[j].lo, lA[j].hi, sa);
+            const uint32_t a1 = prmt(lB[j].lo, lB[j].hi, sb);
+            const uint32_t a2 = prmt(lA[j].lo, lA[j].hi, sa >> 16);
+            const uint32_t a3 = prmt(lB[j].lo, lB[j].hi, sb >> 16);
             mma_f16_16816(sc[j][p & 1], a0, a1, a2, a3, Q.qf[4 * wd + p][0], Q.qf[4 * wd + p][1]);
           }
         }

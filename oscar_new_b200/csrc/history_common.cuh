@@ -118,9 +118,9 @@ OSCAR_DEVINL KeyLut key_lut(uint32_t sz) {
   return k;
 }
 
-// PRMT selector of the two codes in bits 0-1 of bytes 0 and 1 of x (one IMAD): nibbles
-// (c0, 4 + c0, c1, 4 + c1) fetch the two fp16 levels from (lo, hi).
-OSCAR_DEVINL uint32_t lut_sel_lo(uint32_t x) { return x * 0x11u + 0x4040u; }
+// PRMT selectors: for codes in bits 0-1 of each byte of x, x * 0x11 + 0x40404040 holds
+// the nibbles (c0, 4 + c0, c1, 4 + c1) in its low half and (c2, 4 + c2, c3, 4 + c3) in
+// its high half; (c, 4 + c) fetches level c from (lo, hi).
 
 // tcgen05 history kernel (history_tc.cu); OSCAR_ERR_UNSUPPORTED for geometries it does
 // not cover (more than 32 query rows per KV head, other slot sizes).
