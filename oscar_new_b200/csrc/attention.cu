@@ -3,10 +3,11 @@
 // BF16 window store (:544-620) and the compact task table (:222-287).
 //
 // History kernel (INT2, rotated space).  One CTA = one (task, split, head group).
-// Lane 0 of warp 0 streams chunks of the paged K stripe (at most one 128-token kernel
-// block) into a 3- or 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk,
-// mbarrier completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast),
-// between its own chunks (there is no separate producer warp).  The warps own (KV head,
+// The warps stream chunks of the paged K stripe (at most one 128-token kernel block)
+// into a 3- or 4-stage shared-memory ring with 1-D bulk copies (cp.async.bulk, mbarrier
+// completion; contiguous [chunk tokens x heads x 160 B] runs, no multicast); the copy
+// of chunk c + stages - 1 is issued by warp c % warps after its part of chunk c (there
+// is no separate producer warp).  The warps own (KV head,
 // 8 query rows) units and two 16-token m-tiles each.  Narrow launches (all KV heads x
 // row tiles in 4 warps) run 3 CTAs per SM at <= 168 registers, wider ones 8 warps per
 // CTA at up to 255 registers.
@@ -147,12 +148,11 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
 
   const int hpc = P.heads_per_cta;
   const int token_bytes = hpc * g.slot_bytes;
-  // Copies are issued by lane 0 of warp 0 between its own chunks: chunk c + STAGES - 1
-  // as soon as the consumers have released its stage (non-blocking probe), and chunk c
-  // at the latest before warp 0 needs it (bounded blocking wait).  Keeping the CTA at
-  // 8 warps (2 per scheduler) leaves each thread up to 255 registers.
+  // Copies: thread 0 issues chunks 0 .. STAGES-2; then, after its own part of chunk c,
+  // warp c % consumers issues chunk c + STAGES - 1 into the stage chunk c - 1 used
+  // (bounded wait for its release).  Rotating the issuer keeps any one warp from being
+  // the slowest of the CTA, which every stage release waits for.
   const int32_t *trow = P.table + (int64_t)ti.req * g.table_stride;
-  int issued = 0;
   auto issue_one = [&](int c) {
     const int s = c % STAGES;
     const int pos = (first_chunk + c) * CT;
@@ -168,20 +168,10 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
         bulk_copy_g2s(dst + tk * token_bytes, src + (int64_t)tk * g.kv_heads * g.slot_bytes, token_bytes, &full[s]);
     }
   };
-  // returns false when a bounded wait for a free stage gave up
-  auto pump = [&](int c) -> bool {
-    while (issued <= c && issued < nchunks) {
-      if (issued >= STAGES && !mbar_wait_bounded(&empty[issued % STAGES], ((issued / STAGES) - 1) & 1))
-        return false;
-      issue_one(issued++);
-    }
-    while (issued < nchunks && issued < c + STAGES) {
-      if (issued >= STAGES && !mbar_test(&empty[issued % STAGES], ((issued / STAGES) - 1) & 1)) break;
-      issue_one(issued++);
-    }
-    return true;
-  };
   if (warp >= P.consumers) return;
+  if (threadIdx.x == 0)
+    for (int c = 0; c < min(STAGES - 1, nchunks); ++c) issue_one(c);
+  int last_issued = -1;
 
   // ---------------- consumer warps ----------------
   const int unit = warp % P.units, sub = warp / P.units;
@@ -205,15 +195,6 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
 #pragma unroll 1
   for (int c = 0; c < nchunks && ok; ++c) {
     const int s = c % STAGES;
-    if (warp == 0) {
-      bool pumped = true;
-      if (lane == 0) pumped = pump(c);
-      if (!__shfl_sync(0xffffffffu, (int)pumped, 0)) {
-        ok = false;
-        if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
-        break;
-      }
-    }
     if (!mbar_wait_bounded(&full[s], (c / STAGES) & 1)) {
       ok = false;
       if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
@@ -362,9 +343,27 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
         }
       }
     }
+    {
+      // copy issue rotates over the warps: after its part of chunk c, warp c % consumers
+      // issues chunk c + STAGES - 1 into the stage that chunk c - 1 used
+      const int cn = c + STAGES - 1;
+      int good = 1;
+      if (warp == c % P.consumers && lane == 0 && cn < nchunks) {
+        if (cn >= STAGES && !mbar_wait_bounded(&empty[cn % STAGES], ((cn / STAGES) - 1) & 1)) {
+          good = 0;
+          if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
+        } else {
+          issue_one(cn);
+          last_issued = cn;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, good, 0)) ok = false;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
+  if (!ok && lane == 0 && last_issued >= 0)
+    (void)mbar_wait_bounded(&full[last_issued % STAGES], (last_issued / STAGES) & 1);  // let it land
 
   // ---------------- combine the warps of a unit, write the partial ----------------
 #pragma unroll
