@@ -220,6 +220,23 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
       uint32_t kaw[NM][4], kbw[NM][4];
       KeyLut lA[NM], lB[NM];
       uint32_t vsz[NM][2];
+      static_assert(NM == 2, "one key table per lane covers two 16-token m-tiles");
+      {
+        // lane 4gi + 2j + h builds the table of token (m-tile j, row gi + 8h) once; the
+        // four lanes of row group gi fetch the four tables they use
+        const uint8_t *own = ((t >> 1) ? tl[1] : tl[0]) + (gi + 8 * (t & 1)) * token_bytes;
+        const KeyLut mine = key_lut(*reinterpret_cast<const uint32_t *>(own + 64));
+#pragma unroll
+        for (int j = 0; j < NM; ++j) {
+          const int la = 4 * gi + 2 * j;
+          lA[j].lo = __shfl_sync(0xffffffffu, mine.lo, la);
+          lA[j].hi = __shfl_sync(0xffffffffu, mine.hi, la);
+          lA[j].inv = __shfl_sync(0xffffffffu, mine.inv, la);
+          lB[j].lo = __shfl_sync(0xffffffffu, mine.lo, la + 1);
+          lB[j].hi = __shfl_sync(0xffffffffu, mine.hi, la + 1);
+          lB[j].inv = __shfl_sync(0xffffffffu, mine.inv, la + 1);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < NM; ++j) {
         const uint8_t *ra = tl[j] + gi * token_bytes, *rb = ra + 8 * token_bytes;
@@ -227,8 +244,6 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
         const uint4 kb = *reinterpret_cast<const uint4 *>(rb + 16 * t);
         kaw[j][0] = ka.x, kaw[j][1] = ka.y, kaw[j][2] = ka.z, kaw[j][3] = ka.w;
         kbw[j][0] = kb.x, kbw[j][1] = kb.y, kbw[j][2] = kb.z, kbw[j][3] = kb.w;
-        lA[j] = key_lut(*reinterpret_cast<const uint32_t *>(ra + 64));
-        lB[j] = key_lut(*reinterpret_cast<const uint32_t *>(rb + 64));
         vsz[j][0] = *reinterpret_cast<const uint32_t *>(ra + g.vector_bytes + 64);
         vsz[j][1] = *reinterpret_cast<const uint32_t *>(rb + g.vector_bytes + 64);
       }
