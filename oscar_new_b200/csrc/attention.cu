@@ -38,6 +38,10 @@ constexpr int kMaxConsumerWarps = 8;  // wider CTAs spill the O accumulator
 // 8 hide more of the operand-building latency).
 constexpr int kNarrowWarps = 4;
 constexpr int kNarrowCtasPerSm = 3;
+// Middle launch (all KV heads x row tiles of a task in at most 12 warps, e.g. MTP verify
+// with 3 row tiles x 4 KV heads): one 12-warp CTA per SM at <= 170 registers, every KV
+// head in the CTA so each chunk is one contiguous copy.
+constexpr int kMidWarps = 12;
 // Query operands of one 8-row n-tile for the fp16 key MMAs, in the contraction order
 // the key tables are read in (lane t owns dims [64t, 64t+64); k16-step j = 4w + p covers
 // dims 16(4t+w) + {p, 4+p} in the first register and 16(4t+w) + {8+p, 12+p} in the
@@ -1057,7 +1061,8 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) 
   if (P.ntiles > kMaxConsumerWarps) return OSCAR_ERR_UNSUPPORTED;
   constexpr int NM = 2;
   const bool narrow = P.ntiles * g.kv_heads <= kNarrowWarps;
-  const int max_warps = narrow ? kNarrowWarps : kMaxConsumerWarps;
+  const bool mid = !narrow && P.ntiles * g.kv_heads <= kMidWarps;
+  const int max_warps = narrow ? kNarrowWarps : (mid ? kMidWarps : kMaxConsumerWarps);
   int hpc = g.kv_heads;
   while (hpc * P.ntiles > max_warps) hpc = (hpc + 1) / 2;
   if (g.kv_heads % hpc) hpc = 1;
@@ -1075,9 +1080,8 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) 
   if (smem < 128 + xch) smem = 128 + xch;
   if (smem > 227 * 1024) return OSCAR_ERR_UNSUPPORTED;
   dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
-  if (narrow) {
-    return launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream);
-  }
+  if (narrow) return launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream);
+  if (mid) return launch_history<kMidWarps, NM, 4, 1>(P, grid, smem, stream);
   return launch_history<kMaxConsumerWarps, NM, 4, 1>(P, grid, smem, stream);
 }
 
