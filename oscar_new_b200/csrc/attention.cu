@@ -778,12 +778,11 @@ struct FinalParams {
   __nv_bfloat16 *out;
 };
 
-// 8 output rows per CTA on a 16-row GEMM tile (rows 8..15 of the tile are zero), 4 warps:
-// a decode step (n * Hq rows) spreads over n * Hq / 8 CTAs.  Each warp merges two rows
-// with the loads of both rows in flight together (the merge is latency-bound: a row
-// reads one 1 KB partial per used split).
+// 4 output rows per CTA on a 16-row GEMM tile (rows 4..15 of the tile are zero), 4 warps,
+// one row each: a decode step (n * Hq rows) spreads over n * Hq / 4 CTAs (the merge is
+// latency-bound: a row reads one 1 KB partial per used split, four at a time).
 constexpr int kFinRows = 16;
-constexpr int kFinLive = 8;
+constexpr int kFinLive = 4;
 constexpr int kFinThreads = 128;
 constexpr int kFinSmem = (kFinRows * kDim + 2 * kBStageElems) * 2 + 2 * kFinRows * 4;
 
@@ -876,8 +875,9 @@ __global__ void __launch_bounds__(kFinThreads) finalize_kernel(FinalParams P) {
   rowgemm_mainloop<1, kFinThreads>(acc, sA, sB, BMatrix{P.rv, 1, 256});  // B(k, n) = Rv[n][k]
   const int wn = warp & 3, gq = lane >> 2, t = lane & 3;
   {
-    const int hb = 0;  // tile rows 0..7 are this CTA's rows
+    const int hb = 0;  // tile rows 0..kFinLive-1 are this CTA's rows
     const int r = gq;
+    if (r >= kFinLive) return;
     const int64_t row = row0 + r;
     if (row >= P.rows) return;
     const float xa = s_la[r], xb = s_lb[r];
