@@ -1042,12 +1042,11 @@ static int sm_count() {
   return cache[dev];
 }
 
+// Opt-in switch for the tcgen05 history kernel, read at every launch (a getenv is far
+// below a launch's cost) so that one process can compare both paths.
 static bool history_tc_enabled() {
-  static const bool on = [] {
-    const char *v = getenv("OSCAR_HISTORY_TC");
-    return v != nullptr && v[0] == '1';
-  }();
-  return on;
+  const char *v = getenv("OSCAR_HISTORY_TC");
+  return v != nullptr && v[0] == '1';
 }
 
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) {
