@@ -26,6 +26,7 @@
 // MMAs use the swapped orientation (tokens / dims as M = 16, query rows as N = 8).
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #include "history_common.cuh"
 #include "rowgemm.cuh"
@@ -1019,10 +1020,24 @@ static bool geo_ok(const oscar_geometry &g) {
          g.recent >= 0 && g.query_tile > 0 && g.table_stride > 0;
 }
 
+// priority != 0: launch priority of the grid (the decode step gives the history grid the
+// device's greatest priority, so a concurrently queued lower-priority grid only takes
+// the SM slots that history blocks leave free, i.e. the tail of the last wave)
 template <int MAXW, int NM, int STAGES, int MINB>
-static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStream_t stream) {
+static int launch_history(const HistParams &P, dim3 grid, size_t smem, cudaStream_t stream, int priority) {
   if (!ensure_dynamic_smem<history_attention_kernel<MAXW, NM, STAGES, MINB>>(smem)) return OSCAR_ERR_LAUNCH;
-  history_attention_kernel<MAXW, NM, STAGES, MINB><<<grid, 32 * P.consumers, smem, stream>>>(P);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(32 * P.consumers);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributePriority;
+  attr[0].val.priority = priority;
+  cfg.attrs = attr;
+  cfg.numAttrs = priority != 0 ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, history_attention_kernel<MAXW, NM, STAGES, MINB>, P) != cudaSuccess)
+    return OSCAR_ERR_LAUNCH;
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
 }
@@ -1049,7 +1064,7 @@ static bool history_tc_enabled() {
   return v != nullptr && v[0] == '1';
 }
 
-static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) {
+static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {
   if (history_tc_enabled()) {
     const int rc = history_tc_launch(P, num_tasks, stream);
     if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
@@ -1079,9 +1094,40 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream) 
   if (smem < 128 + xch) smem = 128 + xch;
   if (smem > 227 * 1024) return OSCAR_ERR_UNSUPPORTED;
   dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
-  if (narrow) return launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream);
-  if (mid) return launch_history<kMidWarps, NM, 4, 1>(P, grid, smem, stream);
-  return launch_history<kMaxConsumerWarps, NM, 4, 1>(P, grid, smem, stream);
+  if (narrow) return launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream, priority);
+  if (mid) return launch_history<kMidWarps, NM, 4, 1>(P, grid, smem, stream, priority);
+  return launch_history<kMaxConsumerWarps, NM, 4, 1>(P, grid, smem, stream, priority);
+}
+
+// Side stream of the decode step's BF16 raw path (one per device, created on first use):
+// the raw grid is small and latency-bound, so it runs beside the history grid, which
+// gets the greatest launch priority; `mu` keeps the fork / launch / join sequence of
+// concurrent host callers on one device from interleaving on the shared events.
+struct RawSide {
+  std::once_flag once;
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  int priority = 0;
+  bool ok = false;
+};
+
+static RawSide *raw_side() {
+  static RawSide cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  RawSide &c = cache[dev];
+  std::call_once(c.once, [&c] {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return;
+    if (cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess) return;
+    if (cudaEventCreateWithFlags(&c.fork, cudaEventDisableTiming) != cudaSuccess) return;
+    if (cudaEventCreateWithFlags(&c.join, cudaEventDisableTiming) != cudaSuccess) return;
+    c.priority = greatest;
+    c.ok = true;
+  });
+  if (!c.ok) cudaGetLastError();  // a failed set-up leaves the single-stream order
+  return c.ok ? &c : nullptr;
 }
 
 static int raw_launch(const RawParams &P, int32_t num_tasks, cudaStream_t stream) {
@@ -1236,7 +1282,16 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     H.scale_log2 = scale * kLog2e;
     H.balanced = 1;
     H.target_ctas = 8 * sm_count();
-    int rc = history_launch(H, num_tasks, st);
+    // history on the caller's stream at the greatest priority, the raw path beside it on
+    // the side stream (joined before the merge); without a side stream, one after the other
+    RawSide *side = raw_side();
+    std::unique_lock<std::mutex> side_lock;
+    if (side) {
+      side_lock = std::unique_lock<std::mutex>(side->mu);
+      if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess)
+        return OSCAR_ERR_LAUNCH;
+    }
+    int rc = history_launch(H, num_tasks, st, side ? side->priority : 0);
     if (rc) return rc;
     RawParams R{};
     R.query = reinterpret_cast<const __nv_bfloat16 *>(query);
@@ -1251,8 +1306,11 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     R.geo = geo;
     R.scale_log2 = scale * kLog2e;
     R.ntiles = (geo.query_tile * geo.group + 7) / 8;
-    rc = raw_launch(R, num_tasks, st);
+    rc = raw_launch(R, num_tasks, side ? side->stream : st);
     if (rc) return rc;
+    if (side && (cudaEventRecord(side->join, side->stream) != cudaSuccess ||
+                 cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess))
+      return OSCAR_ERR_LAUNCH;
   }
   if (!ensure_dynamic_smem<finalize_kernel>(kFinSmem)) return OSCAR_ERR_LAUNCH;
   FinalParams F{};
