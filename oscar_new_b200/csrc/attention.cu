@@ -1270,6 +1270,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
   if (qs0 % 8 || qs1 % 8 || ks0 % 8 || ks1 % 8 || vs0 % 8 || vs1 % 8) return OSCAR_ERR_INVALID;
   cudaStream_t st = (cudaStream_t)stream;
   const int hq = geo.kv_heads * geo.group;
+  bool window_done = false;
   if (num_tasks > 0) {
     HistParams H{};
     H.query = reinterpret_cast<const __nv_bfloat16 *>(qrot);
@@ -1282,8 +1283,9 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     H.scale_log2 = scale * kLog2e;
     H.balanced = 1;
     H.target_ctas = 8 * sm_count();
-    // history on the caller's stream at the greatest priority, the raw path beside it on
-    // the side stream (joined before the merge); without a side stream, one after the other
+    // history on the caller's stream at the greatest priority, the raw path and then the
+    // window store beside it on the side stream (joined before the merge); without a side
+    // stream, one after the other
     RawSide *side = raw_side();
     std::unique_lock<std::mutex> side_lock;
     if (side) {
@@ -1308,6 +1310,14 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     R.ntiles = (geo.query_tile * geo.group + 7) / 8;
     rc = raw_launch(R, num_tasks, side ? side->stream : st);
     if (rc) return rc;
+    if (side && window_programs > 0) {
+      // the window store overwrites ring slots the raw path reads: after it, same stream
+      window_store_kernel<<<window_programs, 256, 0, side->stream>>>(
+          reinterpret_cast<const __nv_bfloat16 *>(key), ks0, ks1, reinterpret_cast<const __nv_bfloat16 *>(value),
+          vs0, vs1, reinterpret_cast<__nv_bfloat16 *>(window), qstarts, seq_lens, table, counts, geo);
+      OSCAR_CHECK_LAUNCH();
+      window_done = true;
+    }
     if (side && (cudaEventRecord(side->join, side->stream) != cudaSuccess ||
                  cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess))
       return OSCAR_ERR_LAUNCH;
@@ -1320,7 +1330,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
   F.out = reinterpret_cast<__nv_bfloat16 *>(output);
   finalize_kernel<<<(unsigned)((F.rows + kFinLive - 1) / kFinLive), kFinThreads, kFinSmem, st>>>(F);
   OSCAR_CHECK_LAUNCH();
-  if (window_programs > 0) {
+  if (window_programs > 0 && !window_done) {
     window_store_kernel<<<window_programs, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16 *>(key), ks0, ks1, reinterpret_cast<const __nv_bfloat16 *>(value), vs0,
         vs1, reinterpret_cast<__nv_bfloat16 *>(window), qstarts, seq_lens, table, counts, geo);
