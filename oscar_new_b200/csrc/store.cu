@@ -39,6 +39,10 @@ __global__ void __launch_bounds__(256) store_int2_kernel(const __nv_bfloat16 *__
   }
 }
 
+// Decode-sized store jobs: 8 live rows on the 16-row GEMM tile, so that each of the 4
+// warps quantises one pair of rows (the quantiser, not the GEMM, is the critical path).
+constexpr int kSmallStoreRows = 8;
+
 template <int ROWS>
 __global__ void __launch_bounds__(ROWS == 64 ? 256 : 128) rotate_kernel(RotateParams p) {
   constexpr int MI = ROWS == 64 ? 2 : 1;
@@ -55,7 +59,9 @@ __global__ void __launch_bounds__(ROWS == 64 ? 256 : 128) rotate_kernel(RotatePa
   }
   const RotateJob job = p.job[j];
   const int64_t nrows = job.n * job.h;
-  const int64_t row0 = tile * ROWS;
+  // store jobs of the 16-row kernel keep 8 live rows per tile (one quantise pass per warp)
+  const int live = (ROWS == 16 && job.kv >= 0) ? kSmallStoreRows : ROWS;
+  const int64_t row0 = tile * live;
   load_a_tile<ROWS, NT>(sA, row0, nrows, [&](int64_t r) {
     return job.x + (r / job.h) * job.s0 + (r % job.h) * job.s1;
   });
@@ -65,7 +71,7 @@ __global__ void __launch_bounds__(ROWS == 64 ? 256 : 128) rotate_kernel(RotatePa
   // acc -> bf16 tile (rounded exactly once, as the reference rotate output)
   store_acc_bf16<MI>(sA, acc);
   __syncthreads();
-  rotate_epilogue(sA, ROWS, row0, job, p, NW);
+  rotate_epilogue(sA, live, row0, job, p, NW);
 }
 
 // Large row counts go to the tcgen05 kernel; 16-row tiles (4x the CTAs of 64-row ones)
@@ -82,7 +88,8 @@ static int launch_rotate(RotateParams p, cudaStream_t stream) {
   const int rows = small ? 16 : 64;
   int64_t total = 0;
   for (int j = 0; j < p.njobs; ++j) {
-    p.job[j].tiles = (p.job[j].n * p.job[j].h + rows - 1) / rows;
+    const int jr = (small && p.job[j].kv >= 0) ? kSmallStoreRows : rows;
+    p.job[j].tiles = (p.job[j].n * p.job[j].h + jr - 1) / jr;
     total += p.job[j].tiles;
   }
   const int smem = (rows * kDim + 2 * kBStageElems) * 2;
