@@ -339,6 +339,11 @@ def test_attention_partials_match_reference_kernel(cuda_lib, index):
         ("ragged_overlap", [69, 263], [4, 3], 6, 1, make_config(64, 256, 3), 16),
         # skewed lengths: balanced splits give the long request most of the 64 splits
         ("skewed_balanced", [140, 9000, 333, 2, 1500], [4, 4, 1, 2, 4], 24, 4, make_config(4, 128, 3), 64),
+        # launch shapes: 8 KV heads x 2 row tiles (8-warp CTAs), 2 KV heads x 3 row tiles
+        # (12-warp CTA, two warps per unit), 8 row tiles per KV head (GQA 16 at MTP verify)
+        ("wide_8heads", [1300, 2600], [4, 4], 32, 8, make_config(4, 128, 3), 8),
+        ("mid_2heads", [1100, 3100], [4, 3], 12, 2, make_config(4, 128, 3), 8),
+        ("group16_mtp", [800, 1900], [4, 4], 32, 2, make_config(4, 128, 3), 4),
     ],
 )
 def test_decode_step_matches_hybrid_reference(cuda_lib, name, seq, qlen, hq, h, cfg, splits):
