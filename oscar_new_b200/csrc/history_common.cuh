@@ -1,8 +1,8 @@
 // Definitions shared by the two INT2 history attention kernels (attention.cu:
 // mma.sync with register-built operands; history_tc.cu: tcgen05 with the key
 // operands in tensor memory): launch parameters, task decoding (reference
-// oscar_ascend/kernels.py:290-330) and the per-token coefficients of the
-// bf16-rounded key.
+// oscar_ascend/kernels.py:290-330), the per-token coefficients of the bf16-rounded key
+// (tcgen05 kernel) and the per-token byte tables of its four levels (mma.sync kernel).
 #pragma once
 
 #include "common.cuh"
@@ -67,10 +67,11 @@ OSCAR_DEVINL TaskInfo load_task(int task, const int32_t *tasks, const int32_t *t
 }
 
 // Per-token coefficients of q.k with k = bf16(c*s + z) (the reference rounds the
-// dequantised key to bf16):  q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
+// dequantised key to bf16), as the tcgen05 kernel uses them:
+//   q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
 // with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.  Since
-// sum(q c) = sum(q b0) + 2 sum(q b1), the kernel uses M = sum(q c) (exact fp16 MMA) and
-// the two low-precision int8 sums A = sum(q b0), C = sum(q b0 b1):
+// sum(q c) = sum(q b0) + 2 sum(q b1), with the three MMA sums M = sum(q c),
+// A = sum(q b0), C = sum(q b0 b1) over the code, b0 and b0b1 planes:
 //   q.k = v0*sum(q) + (d1 + a/2) M - (a/2) A + b C.
 struct KeyCoef {
   float v0, d1, a, b;
