@@ -8,21 +8,20 @@
 //   out of the [pages][page tokens][heads x 160 B] history stripe: the head's slots,
 //   strided in HBM, land contiguous in shared memory) into a 4-stage ring.  No multicast.
 // * Warps 0-3 ("key warps", thread = token = TMEM lane) expand the token's 2-bit key
-//   codes into three fp16 A operands in tensor memory: the code c and the bits b0 and
-//   b0*b1 at each of the four positions of a byte, as the exact subnormals
-//   {c, b0, b0 b1} * 4^p * 2^-24 (one AND per two codes).  One thread issues 48
-//   tcgen05.mma (M = 128 tokens, N = 16 or 32 query rows, K = 16) against a single
-//   query tile B (q / 4^p, fp16, 128-byte swizzle) in shared memory: all query rows of
-//   the task share the operand work.  The key warps read the three accumulators back
-//   and form the logit of the bf16-rounded key exactly as the mma.sync kernel does:
-//     q.k = v0 sum(q) + (d1 + a/2) sum(q c) - (a/2) sum(q b0) + b sum(q b0 b1),
-//   then the online softmax (log2 domain, lazy re-basing), writing P' = p * s_v as fp16
-//   and the re-basing factors to shared memory.
+//   codes into one fp16 A operand in tensor memory: the token's four bf16 key levels
+//   (exact in fp16 after a power-of-two scale) looked up by PRMT, two codes per
+//   instruction, 128 columns.  One thread issues 16 tcgen05.mma (M = 128 tokens, N = 16
+//   or 32 query rows, K = 16) against a single query tile B (q times a per-row power
+//   of two, fp16, 128-byte swizzle) in shared memory: all query rows of the task share
+//   the operand work.  The key warps read the accumulators back (logit = D * 2^-e_token *
+//   2^-e_row), take each row's warp maximum with one integer reduction, run the online
+//   softmax (log2 domain, lazy re-basing) and write P' = p * s_v as fp16 and the
+//   re-basing factors to shared memory.
 // * Warps 4-7 ("value warps") each own 64 of the 256 dims: O^T += Vc^T . P'^T on
 //   mma.sync m16n8k16 with the V codes as fp16 subnormals (byte pairs of two tokens by
 //   prmt, one AND per two codes) for every 8-row tile of the task's query rows.
-// Tensor memory: 3 x 128 columns of A operands + 3 x N accumulator columns (512
-// allocated, one CTA per SM).  Every mbarrier wait is bounded; a timeout sets the
+// Tensor memory: 128 columns of A operand + N accumulator columns (256 allocated, one
+// CTA per SM).  Every mbarrier wait is bounded; a timeout sets the
 // status word, the warps leave their loops at the next common point and the CTA frees
 // its tensor memory.
 #include <cstring>
@@ -40,8 +39,8 @@ constexpr int kTcStageBytes = kTcTile * kTcSlot;  // 20 KiB
 constexpr int kTcThreads = 256;
 constexpr int kTcMaxRows = 32;
 constexpr int kPRowBytes = kTcTile * 2 + 16;  // P' row: 128 fp16 + 16 B pad (ldmatrix rows hit distinct banks)
-constexpr int kColX0 = 128, kColX01 = 256, kColD = 384;
-constexpr uint32_t kTcTmemCols = 512;
+constexpr int kColD = 128;  // A operand (key levels) in columns 0..127, accumulators after it
+constexpr uint32_t kTcTmemCols = 256;
 constexpr int kOffB = kTcStages * kTcStageBytes;               // query tile (1024-aligned)
 constexpr int kOffP = kOffB + kTcMaxRows * kDim * 2;           // P' double buffer
 constexpr int kOffSmall = kOffP + 2 * kTcMaxRows * kPRowBytes;  // scalars and barriers
@@ -49,7 +48,8 @@ constexpr int kOffSmall = kOffP + 2 * kTcMaxRows * kPRowBytes;  // scalars and b
 struct TcSmall {
   float alpha[2][kTcMaxRows];
   float mrun[2][kTcMaxRows];
-  float qsum[kTcMaxRows];
+  float qup[kTcMaxRows];  // per-row power-of-two scale of the fp16 query tile
+  float qm[kTcMaxRows];   // its inverse times log2(e) * softmax scale
   float wmax[4][kTcMaxRows];
   float wl[4][kTcMaxRows];
   float wz[4][kTcMaxRows];
@@ -145,23 +145,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
   }
   if (tid < kTcMaxRows) S.mrun[0][tid] = -INFINITY;
   if (warp == 0) tmem_alloc(&S.tmem, kTcTmemCols);
-  // query tile B: row n, contraction index k = 16 j + 4 p + 2 s + h holds q[16 j + 4 s + p + 8 h] / 4^p
-  // (the order the key codes are expanded in), K-major in four 64-wide blocks, 128-byte swizzle
+  // per-row scale of the query: max |q| into [2^14, 2^15), exact in fp16
+  if (tid < kTcMaxRows) {
+    float amax = 0.f;
+    if (tid < R) {
+      const uint16_t *qrow = reinterpret_cast<const uint16_t *>(
+          P.query + (int64_t)(ti.qstart + ti.qoff + tid / g.group) * P.qs0 +
+          (int64_t)(head * g.group + tid % g.group) * P.qs1);
+      for (int d = 0; d < kDim; ++d) amax = fmaxf(amax, fabsf(bf16_bits_to_float(qrow[d])));
+    }
+    const uint32_t ex = (__float_as_uint(amax) >> 23) & 0xffu, exc = ex < 16u ? 16u : ex;
+    S.qup[tid] = amax > 0.f ? __uint_as_float((268u - exc) << 23) : 0.f;
+    S.qm[tid] = amax > 0.f ? __uint_as_float((exc - 14u) << 23) * P.scale_log2 : 0.f;
+  }
+  __syncthreads();
+  // query tile B: row n, contraction index k = 16 W + 4 p + 2 h + s holds q[16 W + p + 8 h + 4 s]
+  // (the order the key levels are expanded in: column 8 W + 2 p + h of the A operand
+  // holds the levels of code position p of bytes {2h, 2h + 1} of word W), K-major in four
+  // 64-wide blocks, 128-byte swizzle
   for (int e = tid; e < N * 32; e += kTcThreads) {
     const int n = e >> 5, ch = e & 31;
     uint32_t wv[4] = {0u, 0u, 0u, 0u};
     if (n < R) {
       const uint16_t *qrow = reinterpret_cast<const uint16_t *>(
           P.query + (int64_t)(ti.qstart + ti.qoff + n / g.group) * P.qs0 + (int64_t)(head * g.group + n % g.group) * P.qs1);
+      const float up = S.qup[n];
 #pragma unroll
       for (int e2 = 0; e2 < 4; ++e2) {
         float v2[2];
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int k = 8 * ch + 2 * e2 + h2;
-          const int p = (k >> 2) & 3;
-          const int dim = 16 * (k >> 4) + 4 * ((k >> 1) & 1) + p + 8 * (k & 1);
-          v2[h2] = bf16_bits_to_float(qrow[dim]) * (1.0f / (float)(1 << (2 * p)));
+        for (int s2 = 0; s2 < 2; ++s2) {
+          const int k = 8 * ch + 2 * e2 + s2;
+          const int dim = 16 * (k >> 4) + ((k >> 2) & 3) + 8 * ((k >> 1) & 1) + 4 * (k & 1);
+          v2[s2] = bf16_bits_to_float(qrow[dim]) * up;
         }
         wv[e2] = pack_half2(v2[0], v2[1]);
       }
@@ -169,16 +185,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
     const int kb = ch >> 3, c = ch & 7;
     *reinterpret_cast<uint4 *>(smem + kOffB + kb * (N * 128) + n * 128 + ((c ^ (n & 7)) << 4)) =
         make_uint4(wv[0], wv[1], wv[2], wv[3]);
-  }
-  if (tid < kTcMaxRows) {
-    float s = 0.f;
-    if (tid < R) {
-      const uint16_t *qrow = reinterpret_cast<const uint16_t *>(
-          P.query + (int64_t)(ti.qstart + ti.qoff + tid / g.group) * P.qs0 +
-          (int64_t)(head * g.group + tid % g.group) * P.qs1);
-      for (int d = 0; d < kDim; ++d) s += bf16_bits_to_float(qrow[d]);
-    }
-    S.qsum[tid] = s;
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -193,13 +199,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
     float lp[kTcMaxRows], zp[kTcMaxRows], lg[kTcMaxRows];
 #pragma unroll
     for (int r = 0; r < kTcMaxRows; ++r) lp[r] = zp[r] = 0.f;
-    const float sl2 = P.scale_log2;
     const uint32_t idesc = idesc_f16_m128(N);
     for (int t = 0; t < nblk; ++t) {
       const int s = t % kTcStages, b = t & 1;
       bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&S.full[s], (t / kTcStages) & 1));
       uint32_t w[16];
       uint32_t ksz = 0, vsz = 0;
+      float kinv = 0.f;
       if (ok) {
         const uint8_t *row = smem + s * kTcStageBytes + i * kTcSlot;
 #pragma unroll
@@ -211,27 +217,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
         vsz = *reinterpret_cast<const uint32_t *>(row + 132);
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.empty[s]);
-        // the three A operands: column 8 j + 2 p + s of operand f holds the position-p
-        // codes (f = 0), b0 bits (f = 1) or b0 b1 bits (f = 2) of bytes {s, s + 2} of word j
+        // the A operand: the token's bf16 key levels (exact in fp16 after its power-of-two
+        // scale) through its byte table, column 8 W + 2 p + h = code position p of bytes
+        // {2h, 2h + 1} of word W; one IMAD builds both PRMT selectors of a word position
+        const KeyLut lt = key_lut(ksz);
+        kinv = lt.inv;
 #pragma unroll
-        for (int f = 0; f < 3; ++f) {
+        for (int bt = 0; bt < 4; ++bt) {
+          uint32_t v[32];
 #pragma unroll
-          for (int bt = 0; bt < 4; ++bt) {
-            uint32_t v[32];
+          for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t ww = w[4 * bt + jj];
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              const uint32_t ww = w[4 * bt + jj];
-              const uint32_t src = f == 2 ? (ww & (ww >> 1)) : ww;
-              const uint32_t s8 = src >> 8;
-              const uint32_t m0 = f == 0 ? 0x00030003u : 0x00010001u;
-#pragma unroll
-              for (int p = 0; p < 4; ++p) {
-                v[8 * jj + 2 * p] = src & (m0 << (2 * p));
-                v[8 * jj + 2 * p + 1] = s8 & (m0 << (2 * p));
-              }
+            for (int p = 0; p < 4; ++p) {
+              const uint32_t sel = ((ww >> (2 * p)) & 0x03030303u) * 0x11u + 0x40404040u;
+              v[8 * jj + 2 * p] = prmt(lt.lo, lt.hi, sel);
+              v[8 * jj + 2 * p + 1] = prmt(lt.lo, lt.hi, sel >> 16);
             }
-            tmem_store32(lane_base + (uint32_t)(f * 128 + 32 * bt), v);
           }
+          tmem_store32(lane_base + (uint32_t)(32 * bt), v);
         }
         tmem_store_wait();
       } else {
@@ -246,8 +250,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
         for (int j = 0; j < 16; ++j) {
           const uint64_t bd = smem_desc(smem_u32(smem + kOffB) + (j >> 2) * (N * 128) + (j & 3) * 32, 16, 1024);
           umma_f16_ts(tmem + kColD, tmem + 8 * j, bd, idesc, j > 0 ? 1u : 0u);
-          umma_f16_ts(tmem + kColD + N, tmem + kColX0 + 8 * j, bd, idesc, j > 0 ? 1u : 0u);
-          umma_f16_ts(tmem + kColD + 2 * N, tmem + kColX01 + 8 * j, bd, idesc, j > 0 ? 1u : 0u);
         }
         umma_commit(&S.mma);
       }
@@ -255,32 +257,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
       tc_fence_after();
       const int pos = (first_blk + t) * kTcTile + i;
       const bool valid = pos >= lo && pos < hi;
-      const KeyCoef kc = key_coefficients(ksz);
-      const float cM = (kc.d1 + 0.5f * kc.a) * kTwo24, cA = -0.5f * kc.a * kTwo24, cC = kc.b * kTwo24;
       if (ok) {
 #pragma unroll
         for (int g0 = 0; g0 < kTcMaxRows; g0 += 16) {
           if (g0 < N) {
-            uint32_t dm[16], d0[16], d1[16];
+            uint32_t dm[16];
             tmem_load16(lane_base + (uint32_t)(kColD + g0), dm);
-            tmem_load16(lane_base + (uint32_t)(kColD + N + g0), d0);
-            tmem_load16(lane_base + (uint32_t)(kColD + 2 * N + g0), d1);
 #pragma unroll
             for (int rr = 0; rr < 16; ++rr) {
               const int r = g0 + rr;
-              float dot = kc.v0 * S.qsum[r];
-              dot = fmaf(cM, __uint_as_float(dm[rr]), dot);
-              dot = fmaf(cA, __uint_as_float(d0[rr]), dot);
-              dot = fmaf(cC, __uint_as_float(d1[rr]), dot);
-              lg[r] = (valid && r < R) ? dot * sl2 : -INFINITY;
+              lg[r] = (valid && r < R) ? __uint_as_float(dm[rr]) * (kinv * S.qm[r]) : -INFINITY;
             }
           }
         }
+        // per-row max over the warp's 32 tokens: one integer reduction on an order-preserving
+        // image of the float
 #pragma unroll
         for (int r = 0; r < kTcMaxRows; ++r) {
           if (r >= R) break;
-          const float mx = warp_max(lg[r]);
-          if (lane == 0) S.wmax[warp][r] = mx;
+          const int key = __float_as_int(lg[r]);
+          const int mk = __reduce_max_sync(0xffffffffu, key >= 0 ? key : key ^ 0x7fffffff);
+          if (lane == 0) S.wmax[warp][r] = __int_as_float(mk >= 0 ? mk : mk ^ 0x7fffffff);
         }
       } else {
         atomicExch(&S.abort, 1);
