@@ -70,6 +70,14 @@ typedef struct oscar_clip {
 /* Library/device identification. Returns the compiled SM arch (100 for sm_100a). */
 int oscar_version(void);
 
+/* Self-test of the bounded device waits (no counterpart in the reference, whose
+ * attention kernel was seen to hang its device): launches one thread that waits, with
+ * the same bounded mbarrier wait every kernel here uses, on a barrier phase that nothing
+ * completes, and writes OSCAR_ERR_TIMEOUT to *status (device int32) when the wait gives
+ * up.  A caller can run it to check that a wait which can never be satisfied ends with
+ * an error status, not a hang, and that the context stays usable. */
+int oscar_selftest_bounded_wait(int32_t *status, void *stream);
+
 /* Y[n,h,:] = bf16( bf16(X[n,h,:]) @ bf16(R) ), fp32 accumulation.
  * Replaces reference oscar_ascend/kernels.py:51-66 (rotate / _rotate_kernel). */
 int oscar_rotate(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int64_t xs2,

@@ -165,6 +165,26 @@ using namespace oscar;
 
 extern "C" int oscar_version(void) { return 100; }
 
+// Bounded-wait self-test: one thread waits, with the bounded mbarrier wait that every
+// kernel of this library uses, on a phase that nothing completes, and records
+// OSCAR_ERR_TIMEOUT in *status when the wait gives up.
+__global__ void bounded_wait_selftest_kernel(int32_t *status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);  // one arrival would complete phase 0; none ever comes
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait_bounded(&bar, 0)) *status = OSCAR_ERR_TIMEOUT;
+}
+
+extern "C" int oscar_selftest_bounded_wait(int32_t *status, void *stream) {
+  if (!status) return OSCAR_ERR_INVALID;
+  bounded_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(status);
+  OSCAR_CHECK_LAUNCH();
+  return OSCAR_OK;
+}
+
 extern "C" int oscar_rotate(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int64_t xs2,
                             const void *r, int64_t rs0, int64_t rs1, void *y, void *stream) {
   if (n < 0 || h <= 0 || xs2 != 1 || !y) return OSCAR_ERR_INVALID;

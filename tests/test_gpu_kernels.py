@@ -524,3 +524,23 @@ def test_device_eigensolver_reconstructs_and_matches_eigvalsh(cuda_lib):
     u = r @ co.pbr(256).T @ co.hadamard(256).T
     recon = (u * ev[:, None, :]) @ u.transpose(-1, -2)
     torch.testing.assert_close(recon, cov.double(), atol=2e-4, rtol=2e-3)
+
+
+def test_bounded_wait_times_out_and_context_stays_usable(cuda_lib):
+    """A device wait that nothing can satisfy ends with OSCAR_ERR_TIMEOUT in the status
+    word (no hang), and the context keeps working afterwards."""
+    import time
+
+    from oscar_new_b200 import _lib
+
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    t0 = time.time()
+    _lib.call("oscar_selftest_bounded_wait", status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    elapsed = time.time() - t0
+    assert int(status.item()) == 4, int(status.item())
+    assert elapsed < 60, elapsed
+    x = torch.randn(16, 2, 256).bfloat16().to(DEV)
+    r = rotation(1).bfloat16().to(DEV)
+    torch.testing.assert_close(kernels.rotate(x, r).float(), (x.float() @ r.float()).bfloat16().float(),
+                               atol=0.03125, rtol=0.015)
