@@ -26,6 +26,7 @@
 // MMAs use the swapped orientation (tokens / dims as M = 16, query rows as N = 8).
 #include <algorithm>
 #include <cstdlib>
+#include <atomic>
 #include <mutex>
 
 #include "history_common.cuh"
@@ -1106,18 +1107,30 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, 
 struct RawSide {
   std::once_flag once;
   std::mutex mu;
+  std::atomic<bool> tried{false};
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
   int priority = 0;
   bool ok = false;
 };
 
-static RawSide *raw_side() {
+// `caller` is the stream of the call: while it is being captured into a graph and the
+// side stream does not exist yet, the call goes without it (creating a stream inside a
+// capture could invalidate the capture) and a later eager call creates it.
+static RawSide *raw_side(cudaStream_t caller) {
   static RawSide cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   RawSide &c = cache[dev];
+  if (!c.tried.load(std::memory_order_acquire)) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(caller, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+      cudaGetLastError();
+      return nullptr;
+    }
+  }
   std::call_once(c.once, [&c] {
+    c.tried.store(true, std::memory_order_release);
     int least = 0, greatest = 0;
     if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return;
     if (cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess) return;
@@ -1286,7 +1299,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     // history on the caller's stream at the greatest priority, the raw path and then the
     // window store beside it on the side stream (joined before the merge); without a side
     // stream, one after the other
-    RawSide *side = raw_side();
+    RawSide *side = raw_side(st);
     std::unique_lock<std::mutex> side_lock;
     if (side) {
       side_lock = std::unique_lock<std::mutex>(side->mu);

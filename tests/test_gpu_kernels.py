@@ -544,3 +544,37 @@ def test_bounded_wait_times_out_and_context_stays_usable(cuda_lib):
     r = rotation(1).bfloat16().to(DEV)
     torch.testing.assert_close(kernels.rotate(x, r).float(), (x.float() @ r.float()).bfloat16().float(),
                                atol=0.03125, rtol=0.015)
+
+
+def _capture_first_call_check():
+    """Body of the next test, run in a fresh process: no eager step before the capture."""
+    cfg = make_config(64, 256, 3)
+    sc = Scenario([300, 700], [1, 1], hq=6, h=1, cfg=cfg, seed=12, max_reqs=4)
+    q, k, v = sc.current()
+    m = sc.meta
+    rk, rv = sc.rk.to(DEV).bfloat16(), sc.rv.to(DEV).bfloat16()
+    out = torch.zeros((q.shape[0], 6 * 256), dtype=torch.bfloat16, device=DEV)
+    scratch = kernels.DecodeScratch(q.shape[0], 6, 8, DEV)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs, 4)
+        qrot = kernels.rotate_store(k, v, rk, rv, sc.history, m.slot_mapping, m.counts, sc.layout, query=q)
+        kernels.decode_attention(qrot, q, k, v, sc.history, sc.window, m, sc.layout, 1 / 16, 8, rv, out, scratch)
+    graph.replay()
+    torch.cuda.synchronize()
+    expect, _ = sc.expected()
+    torch.testing.assert_close(out.view(-1, 6, 256).float().cpu(), expect, atol=0.035, rtol=0.04)
+
+
+def test_graph_capture_as_first_decode_call(cuda_lib):
+    """The first decode call of a process may come inside a CUDA-graph capture (an engine
+    can capture before any eager decode step): the step is captured without the side
+    stream, which is only created outside a capture, and replays correctly."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    r = subprocess.run([sys.executable, "-c", "import tests.test_gpu_kernels as t; t._capture_first_call_check()"],
+                       cwd=root, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
