@@ -74,20 +74,15 @@ OSCAR_DEVINL void rotate_epilogue(const __nv_bfloat16 *sY, int rows, int64_t row
       live = slot >= 0;
     }
     if (!__any_sync(0xffffffffu, live)) continue;
-    float x[16];
+    uint32_t w[8];  // dims 16l .. 16l+15 as bf16 pairs
     const int rr = r < rows ? r : 0;
 #pragma unroll
     for (int c2 = 0; c2 < 2; ++c2) {
       const uint4 raw = *reinterpret_cast<const uint4 *>(sY + rr * kDim + (((2 * l + c2) ^ (rr & 7)) << 3));
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        x[8 * c2 + 2 * q] = bf16_bits_to_float(w[q] & 0xffffu);
-        x[8 * c2 + 2 * q + 1] = bf16_bits_to_float(w[q] >> 16);
-      }
+      w[4 * c2] = raw.x, w[4 * c2 + 1] = raw.y, w[4 * c2 + 2] = raw.z, w[4 * c2 + 3] = raw.w;
     }
     uint8_t *dst = live ? p.history + slot_byte_offset(slot, head, p.geo) + job.kv * p.geo.vector_bytes : nullptr;
-    quantize_pack_half(x, p.clip[job.kv], dst, live);
+    quantize_pack_half(w, p.clip[job.kv], dst, live);
   }
 }
 

@@ -199,6 +199,58 @@ def test_rotate_store_prefill_chunk_with_query_tcgen05(cuda_lib):
     _check_store_bytes(history, layout, masked, krot.view(n, h, 256), vrot.view(n, h, 256), cfg)
 
 
+def _edge_rows(gen, count):
+    """[count, 256] fp32 rows that stress the exact quantiser: the middle code boundary
+    at zero (symmetric data), ties at the percentile ranks, constant rows, tiny and
+    huge magnitudes (a minimum below -65504 makes the fp16 zero -inf: every reference
+    code is 0), mixed binades, a lone outlier."""
+    kinds = [
+        lambda: torch.rand(256, generator=gen) * 3 - 1.5,
+        lambda: torch.randint(-4, 5, (256,), generator=gen).float() * 0.25,
+        lambda: torch.full((256,), 0.0),
+        lambda: torch.full((256,), 0.5),
+        lambda: torch.full((256,), -3.0),
+        lambda: torch.full((256,), 1e-12),
+        lambda: torch.randn(256, generator=gen) * 1e-20,
+        lambda: torch.randn(256, generator=gen) * 3000 + 20000,
+        lambda: torch.randn(256, generator=gen) * 3000 - 70000,
+        lambda: torch.randn(256, generator=gen) * 3000 + 70000,
+        lambda: torch.randn(256, generator=gen) * torch.logspace(-6, 4, 256),
+        lambda: torch.cat([torch.full((1,), 5000.0), torch.randn(255, generator=gen) * 1e-3]),
+        lambda: torch.cat([torch.full((24,), -2.0), torch.full((24,), 2.0), torch.randn(208, generator=gen)]),
+        lambda: (torch.arange(256).float().remainder(11) - 5),
+        lambda: torch.randn(256, generator=gen),
+    ]
+    pick = torch.randint(0, len(kinds), (count,), generator=gen)
+    return torch.stack([kinds[int(i)]()[torch.randperm(256, generator=gen)] for i in pick])
+
+
+@pytest.mark.parametrize("n", [600, 3000])  # 16-row mma.sync tiles / tcgen05 tiles
+@pytest.mark.parametrize("kr,vr,mode", [(0.96, 0.92, "percentile"), (0.875, 0.0, "percentile"),
+                                        (1.0, 1.0, "percentile"), (0.96, 0.92, "factor")])
+def test_rotate_store_quantiser_edge_rows(cuda_lib, n, kr, vr, mode):
+    """Identity rotations hand the epilogue the input rows unchanged, so adversarial
+    rows reach the exact quantiser directly; bytes bit-exact vs the oracle."""
+    cfg = replace(OscarConfig(), k_clip_ratio=kr, v_clip_ratio=vr, clip_mode=mode, k_clip_factor=0.9,
+                  v_clip_factor=0.75)
+    h = 4
+    layout = CacheLayout(768, kv_heads=h, config=cfg)
+    gen = torch.Generator().manual_seed(n + int(kr * 100))
+    k = _edge_rows(gen, n * h).view(n, h, 256).bfloat16()
+    v = _edge_rows(gen, n * h).view(n, h, 256).bfloat16()
+    eye = torch.eye(256).bfloat16().to(DEV)
+    pages = (n + 767) // 768 + 1
+    slots = torch.randperm(pages * 768, generator=gen)[:n].long()
+    slots[::97] = -1
+    cache = cache_stripes(pages, 768, h, DEV)
+    history, _ = layout.tensor_views(cache)
+    counts = torch.tensor([1, n], dtype=torch.int32, device=DEV)
+    _, krot, vrot = kernels.rotate_store(k.to(DEV), v.to(DEV), eye, eye, history, slots.to(DEV), counts, layout,
+                                         debug_rotated=True)
+    assert torch.equal(krot.cpu(), k) and torch.equal(vrot.cpu(), v)
+    _check_store_bytes(history, layout, slots, k, v, cfg)
+
+
 def test_rotate_large_column_major_rotation_tcgen05(cuda_lib):
     """Plain rotation with a transposed (column-major) rotation view: the K-major B
     operand path of the tcgen05 kernel; 6 heads per token (126-row tiles)."""
