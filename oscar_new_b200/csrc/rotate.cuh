@@ -35,12 +35,18 @@ struct RotateParams {
   oscar_clip clip[2];
 };
 
+// Byte offset of a slot's head-0 vector pair in the history stripes, -1 for slot < 0.
+OSCAR_DEVINL int64_t slot_base_offset(int64_t slot, const oscar_geometry &g) {
+  return slot < 0 ? -1 : slot_byte_offset(slot, 0, g);
+}
+
 // Epilogue over a staged tile of `rows` rotated rows (swizzled like the A tile, see
 // a_index) starting at global row `row0` (valid while row < nrows): copy to y, then
 // quantise + scatter K / V rows, two rows per warp.  `nw` warps of the CTA take part.
-// `tile_slots` (optional, shared memory) holds the slot of each token of the tile.
+// `tile_bases` (optional, shared memory; row0 then a multiple of h) holds
+// slot_base_offset of each token of the tile.
 OSCAR_DEVINL void rotate_epilogue(const __nv_bfloat16 *sY, int rows, int64_t row0, const RotateJob &job,
-                                  const RotateParams &p, int nw, const int64_t *tile_slots = nullptr) {
+                                  const RotateParams &p, int nw, const int64_t *tile_bases = nullptr) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nt = nw * 32;
   const int64_t nrows = job.n * job.h;
@@ -57,21 +63,28 @@ OSCAR_DEVINL void rotate_epilogue(const __nv_bfloat16 *sY, int rows, int64_t row
   // two rows per warp, one per half-warp (quantize_pack_half); a half whose row is
   // absent or not stored still takes part in the reductions
   const int half = lane >> 4, l = lane & 15;
+  // token / head of row0 + r without a 64-bit division per row: one for the tile, then
+  // floor(t / h) = umulhi(t, floor((2^32 - 1) / h) + 1), exact for t < 2^16
+  const int64_t token0 = row0 / job.h;
+  const int head0 = (int)(row0 - token0 * job.h);
+  const uint32_t hm = job.h > 1 ? 0xffffffffu / (uint32_t)job.h + 1u : 0u;
 #pragma unroll 1
   for (int pr = warp; 2 * pr < rows; pr += nw) {
     const int r = 2 * pr + half;
     const int64_t row = row0 + r;
     bool live = r < rows && row < nrows;
-    int64_t slot = -1;
+    int64_t base = -1;
     int head = 0;
     if (live) {
-      const int64_t token = row / job.h;
-      head = (int)(row % job.h);
-      if (tile_slots != nullptr)
-        slot = tile_slots[r / job.h];  // prefetched for the tile's tokens (-1 when inactive)
+      const uint32_t t = (uint32_t)(head0 + r);
+      const uint32_t tq = job.h > 1 ? __umulhi(t, hm) : t;
+      const int64_t token = token0 + tq;
+      head = (int)(t - tq * (uint32_t)job.h);
+      if (tile_bases != nullptr)
+        base = tile_bases[tq];  // prefetched for the tile's tokens (-1 when not stored)
       else
-        slot = token < active ? p.slots[token] : -1;
-      live = slot >= 0;
+        base = token < active ? slot_base_offset(p.slots[token], p.geo) : -1;
+      live = base >= 0;
     }
     if (!__any_sync(0xffffffffu, live)) continue;
     uint32_t w[8];  // dims 16l .. 16l+15 as bf16 pairs
@@ -81,7 +94,7 @@ OSCAR_DEVINL void rotate_epilogue(const __nv_bfloat16 *sY, int rows, int64_t row
       const uint4 raw = *reinterpret_cast<const uint4 *>(sY + rr * kDim + (((2 * l + c2) ^ (rr & 7)) << 3));
       w[4 * c2] = raw.x, w[4 * c2 + 1] = raw.y, w[4 * c2 + 2] = raw.z, w[4 * c2 + 3] = raw.w;
     }
-    uint8_t *dst = live ? p.history + slot_byte_offset(slot, head, p.geo) + job.kv * p.geo.vector_bytes : nullptr;
+    uint8_t *dst = live ? p.history + base + (int64_t)head * p.geo.slot_bytes + job.kv * p.geo.vector_bytes : nullptr;
     quantize_pack_half(w, p.clip[job.kv], dst, live);
   }
 }

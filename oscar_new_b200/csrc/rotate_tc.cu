@@ -34,7 +34,7 @@ constexpr int kAStageBytes = kTileM * kChunkK * 2;   // 16 KiB
 constexpr int kBStageBytes = kChunkK * kDim * 2;     // 32 KiB
 constexpr int kStageBytesTc = kAStageBytes + kBStageBytes;
 constexpr int kBarrierBytes = 64;
-constexpr int kSlotBytes = kTileM * 8;             // prefetched slot per token of the tile
+constexpr int kSlotBytes = kTileM * 8;             // prefetched slot base offset per token of the tile
 constexpr int kSmemTc = kStagesTc * kStageBytesTc + kBarrierBytes + kSlotBytes + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 256;
 
@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kThreads, 2) rotate_tc_kernel(const __grid_con
   uint64_t *done = empty + kStagesTc;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
   int32_t *abort_flag = reinterpret_cast<int32_t *>(tmem_slot + 1);
-  int64_t *tile_slots = reinterpret_cast<int64_t *>(smem + kStagesTc * kStageBytesTc + kBarrierBytes);
+  int64_t *tile_bases = reinterpret_cast<int64_t *>(smem + kStagesTc * kStageBytesTc + kBarrierBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   int64_t tile = blockIdx.x;
@@ -94,9 +94,10 @@ __global__ void __launch_bounds__(kThreads, 2) rotate_tc_kernel(const __grid_con
   }
   if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
   if (job.kv >= 0 && tid >= 32 && tid < 32 + job.tile_rows / job.h) {
-    // slots of the tile's tokens, loaded while the GEMM runs (-1: not stored)
+    // slot base offsets of the tile's tokens, computed while the GEMM runs (-1: not stored)
     const int64_t token = tile * (job.tile_rows / job.h) + (tid - 32);
-    tile_slots[tid - 32] = token < P.rp.job[j].n && token < P.rp.counts[1] ? P.rp.slots[token] : -1;
+    tile_bases[tid - 32] =
+        token < P.rp.job[j].n && token < P.rp.counts[1] ? slot_base_offset(P.rp.slots[token], P.rp.geo) : -1;
   }
   tc_fence_before();
   __syncthreads();
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 2) rotate_tc_kernel(const __grid_con
   }
   if (!ok) return;
   RotateJob rj = P.rp.job[j];
-  rotate_epilogue(stage_rows, job.tile_rows, tile * job.tile_rows, rj, P.rp, kThreads / 32, tile_slots);
+  rotate_epilogue(stage_rows, job.tile_rows, tile * job.tile_rows, rj, P.rp, kThreads / 32, tile_bases);
 }
 
 // ---- host side ---------------------------------------------------------------
