@@ -10,9 +10,12 @@
 //   (column-major R, e.g. a transposed view, as a K-major one).
 // * Thread 0 issues 16 tcgen05.mma (M=128, N=256, K=16) into 256 TMEM columns and
 //   commits each stage back to the producer through an mbarrier.
-// * Epilogue: 8 warps read the accumulator from TMEM (warp w owns lanes 32(w%4)..,
-//   column half w/4), round to bf16 and stage the rows in shared memory; then the
-//   shared epilogue (rotate.cuh) writes y and quantises K / V rows warp by warp.
+// * Epilogue: warps 0-7 read the accumulator from TMEM (warp w owns lanes 32(w%4)..,
+//   column half w/4), round to bf16 and stage the rows in shared memory; then all 16
+//   warps run the shared epilogue (rotate.cuh), which writes y and quantises K / V
+//   rows, two per warp at a time.  The quantiser is latency-bound (dependent counting
+//   passes), so the extra warps (at most 64 registers each) hide its latency: 16 warps
+//   per CTA took config 2 from 106 to 89 us against 8.
 // About 97 KiB of shared memory and 256 TMEM columns per CTA: two CTAs share an SM, so
 // one CTA's epilogue overlaps the other's loads and MMAs.  No multicast anywhere.
 // Every mbarrier wait is bounded; after a timeout the CTA lets its copies land, frees
@@ -25,7 +28,7 @@
 namespace oscar {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;  // 8 warps drain the accumulator; all 16 quantise
 constexpr int kTileM = 128;
 constexpr int kChunkK = 64;                          // K per stage
 constexpr int kChunks = kDim / kChunkK;              // 4
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 2) rotate_tc_kernel(const __grid_con
   __syncthreads();
   const bool ok = landed && *abort_flag == 0;
   __nv_bfloat16 *stage_rows = reinterpret_cast<__nv_bfloat16 *>(smem);  // 64 KiB of the 96
-  if (ok) {
+  if (ok && warp < 8) {
     const int q = warp & 3, half = warp >> 2;
     const int r = 32 * q + lane;
 #pragma unroll 1
