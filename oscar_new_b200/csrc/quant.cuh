@@ -84,7 +84,9 @@ OSCAR_DEVINL void quantize_pack_warp(float (&x)[8], const oscar_clip &clip, uint
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float q = __fadd_rn(__fdiv_rn(__fsub_rn(x[i], zf), sf), 0.5f);
-    int c = (int)q;  // truncation toward zero (torch .to(int32))
+    // truncation toward zero as torch .to(int32) on the x86 host: NaN and values out of
+    // the int32 range give INT_MIN (code 0), where CUDA's conversion would saturate
+    int c = (q > -2147483904.f && q < 2147483648.f) ? (int)q : INT_MIN;
     c = min(max(c, 0), 3);
     packed |= (uint32_t)c << (2 * i);
   }

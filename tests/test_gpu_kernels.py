@@ -57,6 +57,7 @@ def test_store_int2_bytes_exact(cuda_lib, kr, vr, mode):
     k[2].fill_(1e-12)
     v[3].fill_(-3)
     k[4, 0] = (torch.arange(256).float().remainder(11) - 5).bfloat16()
+    v[5] = (torch.randn(h, 256, generator=gen) * 3000 - 70000).bfloat16()  # fp16 zero -inf: codes 0
     pages = 4
     cache = cache_stripes(pages, 768, h, DEV)
     history, _ = layout.tensor_views(cache)
