@@ -636,10 +636,11 @@ def run_rotate_store(args):
     print(json.dumps(line), flush=True)
 
 
-def config4_state(device, seed=404):
+def config4_state(device, seed=404, nreq=32):
     """Config 4 (MTP verify): 32 requests with qlen 4 (1 + 3 draft tokens) and seq_len
     ~ exp(U(ln 2048, ln 262144)) seeded; S=4, R=128, MTP=3; request 5's last draft has
-    a padded -1 slot and a 33rd, zero-length padded row closes the batch."""
+    a padded -1 slot and a 33rd, zero-length padded row closes the batch.  ``nreq`` < 32
+    keeps the first requests only (small ncu captures)."""
     from oscar_new_b200 import kernels
     from oscar_new_b200.config import OscarConfig
     from oscar_new_b200.layout import CacheLayout
@@ -647,9 +648,9 @@ def config4_state(device, seed=404):
 
     gen = torch.Generator().manual_seed(seed)
     u = torch.rand(32, generator=gen, dtype=torch.float64)
-    seqs = [int(math.exp(math.log(2048) + x * (math.log(262144) - math.log(2048)))) for x in u.tolist()]
+    seqs = [int(math.exp(math.log(2048) + x * (math.log(262144) - math.log(2048)))) for x in u.tolist()][:nreq]
     seqs.append(0)
-    qlens = [4] * 32 + [0]
+    qlens = [4] * nreq + [0]
     cfg = replace(OscarConfig(), sink_tokens=SINK, recent_tokens=RECENT, speculative_tokens=3)
     layout = CacheLayout(BP, kv_heads=H, config=cfg)
     plan = plan_pages(seqs, qlens, BP, seed=seed, max_reqs=34)
@@ -677,7 +678,8 @@ def config4_state(device, seed=404):
             m1.max_num_reqs = 1
             kernels.store_windows(k, v, window, m1, layout)
     meta = plan.meta(device, cfg.queries_per_tile)
-    meta.slot_mapping[5 * 4 + 3] = -1
+    if nreq > 5:
+        meta.slot_mapping[5 * 4 + 3] = -1
     t = sum(qlens)
     q = torch.randn(t, H * G, D, device=device, generator=dgen).bfloat16()
     k = torch.randn(t, H, D, device=device, generator=dgen)
@@ -894,6 +896,22 @@ def profile_only(what):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
+    if what == "mtp-verify":
+        from oscar_new_b200.config import decode_split_cap
+
+        st = config4_state(device, nreq=8)
+        m = st["meta"]
+        t = st["q"].shape[0]
+        splits = decode_split_cap(32, H, 4, t, H * G)
+        kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
+                              st["cfg"].queries_per_tile)
+        qrot = kernels.rotate(st["q"], st["rk"])
+        for _ in range(4):
+            kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                                       1.0 / math.sqrt(D), splits, False)
+        torch.cuda.synchronize(device)
+        print("profile run done: config 4 (8 requests) history")
+        return
     if what == "rotate-store":
         cs = config2_state(device)
         for _ in range(4):
@@ -928,7 +946,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
-    ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store"], default=None,
+    ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store", "mtp-verify"], default=None,
                     help="build the state, run 4 launches of the kernel (or 4 layer steps) and exit")
     ap.add_argument("--workload", choices=["decode", "rotate-store", "mtp-verify", "calibration"], default="decode",
                     help="decode: config 3 (the headline); rotate-store: config 2; mtp-verify: config 4; "

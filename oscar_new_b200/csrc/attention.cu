@@ -44,52 +44,6 @@ constexpr int kNarrowCtasPerSm = 3;
 // with 3 row tiles x 4 KV heads): one 12-warp CTA per SM at <= 170 registers, every KV
 // head in the CTA so each chunk is one contiguous copy.
 constexpr int kMidWarps = 12;
-// Query operands of one 8-row n-tile for the fp16 key MMAs, in the contraction order
-// the key tables are read in (lane t owns dims [64t, 64t+64); k16-step j = 4w + p covers
-// dims 16(4t+w) + {p, 4+p} in the first register and 16(4t+w) + {8+p, 12+p} in the
-// second):
-//  * qf: q * 2^e in fp16 (row max scaled into [2^14, 2^15)), exact for bf16 queries;
-//  * qm: 2^-e * log2(e) * softmax scale of the rows 2t, 2t+1 this lane accumulates.
-struct QueryFrags {
-  uint32_t qf[16][2];
-  float qm[2];
-};
-
-OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, bool valid, float scale_log2) {
-  const int lane = threadIdx.x & 31, t = lane & 3;
-  uint32_t w[32];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 v = valid ? *reinterpret_cast<const uint4 *>(qrow + 64 * t + 8 * c) : make_uint4(0, 0, 0, 0);
-    w[4 * c] = v.x, w[4 * c + 1] = v.y, w[4 * c + 2] = v.z, w[4 * c + 3] = v.w;
-  }
-  auto dim = [&](int d) {  // bf16 value of local dim d (0..63)
-    const uint32_t word = w[d >> 1];
-    return bf16_bits_to_float((d & 1) ? (word >> 16) : (word & 0xffffu));
-  };
-  float amax = 0.f;
-#pragma unroll
-  for (int d = 0; d < 64; ++d) amax = fmaxf(amax, fabsf(dim(d)));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  const uint32_t ex = (__float_as_uint(amax) >> 23) & 0xffu;
-  const uint32_t exc = ex < 16u ? 16u : ex;
-  const bool any = amax > 0.f;
-  const float up = any ? __uint_as_float((268u - exc) << 23) : 0.f;
-  const float down = any ? __uint_as_float((exc - 14u) << 23) * scale_log2 : 0.f;
-#pragma unroll
-  for (int wd = 0; wd < 4; ++wd)
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int d = 16 * wd + p;
-      Q.qf[4 * wd + p][0] = pack_half2(dim(d) * up, dim(d + 4) * up);
-      Q.qf[4 * wd + p][1] = pack_half2(dim(d + 8) * up, dim(d + 12) * up);
-    }
-  // down is a row-gi value on all four t lanes; the S fragment needs rows 2t, 2t+1.
-  Q.qm[0] = __shfl_sync(0xffffffffu, down, 8 * t);
-  Q.qm[1] = __shfl_sync(0xffffffffu, down, 8 * t + 4);
-}
-
 template <int MAXW, int NM, int STAGES, int MINB>
 __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(HistParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1065,9 +1019,21 @@ static bool history_tc_enabled() {
   return v != nullptr && v[0] == '1';
 }
 
+// Opt-in switch for the shared-operand MTP kernel (9..24 rows per KV head), read at
+// every launch: it is parity-green but slower than history_attention_kernel on config 4
+// (its per-head barriers stall more than the shared operands save).
+static bool history_mtp_enabled() {
+  const char *v = getenv("OSCAR_HISTORY_MTP");
+  return v != nullptr && v[0] == '1';
+}
+
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {
   if (history_tc_enabled()) {
     const int rc = history_tc_launch(P, num_tasks, stream);
+    if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
+  }
+  if (history_mtp_enabled()) {
+    const int rc = history_mtp_launch(P, num_tasks, stream, priority);
     if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
   }
   const oscar_geometry &g = P.geo;

@@ -123,8 +123,59 @@ OSCAR_DEVINL KeyLut key_lut(uint32_t sz) {
 // the nibbles (c0, 4 + c0, c1, 4 + c1) in its low half and (c2, 4 + c2, c3, 4 + c3) in
 // its high half; (c, 4 + c) fetches level c from (lo, hi).
 
+// Query operands of one 8-row n-tile for the fp16 key MMAs, in the contraction order
+// the key tables are read in (lane t owns dims [64t, 64t+64); k16-step j = 4w + p covers
+// dims 16(4t+w) + {p, 4+p} in the first register and 16(4t+w) + {8+p, 12+p} in the
+// second):
+//  * qf: q * 2^e in fp16 (row max scaled into [2^14, 2^15)), exact for bf16 queries;
+//  * qm: 2^-e * log2(e) * softmax scale of the rows 2t, 2t+1 this lane accumulates.
+struct QueryFrags {
+  uint32_t qf[16][2];
+  float qm[2];
+};
+
+OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, bool valid, float scale_log2) {
+  const int lane = threadIdx.x & 31, t = lane & 3;
+  uint32_t w[32];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 v = valid ? *reinterpret_cast<const uint4 *>(qrow + 64 * t + 8 * c) : make_uint4(0, 0, 0, 0);
+    w[4 * c] = v.x, w[4 * c + 1] = v.y, w[4 * c + 2] = v.z, w[4 * c + 3] = v.w;
+  }
+  auto dim = [&](int d) {  // bf16 value of local dim d (0..63)
+    const uint32_t word = w[d >> 1];
+    return bf16_bits_to_float((d & 1) ? (word >> 16) : (word & 0xffffu));
+  };
+  float amax = 0.f;
+#pragma unroll
+  for (int d = 0; d < 64; ++d) amax = fmaxf(amax, fabsf(dim(d)));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const uint32_t ex = (__float_as_uint(amax) >> 23) & 0xffu;
+  const uint32_t exc = ex < 16u ? 16u : ex;
+  const bool any = amax > 0.f;
+  const float up = any ? __uint_as_float((268u - exc) << 23) : 0.f;
+  const float down = any ? __uint_as_float((exc - 14u) << 23) * scale_log2 : 0.f;
+#pragma unroll
+  for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int d = 16 * wd + p;
+      Q.qf[4 * wd + p][0] = pack_half2(dim(d) * up, dim(d + 4) * up);
+      Q.qf[4 * wd + p][1] = pack_half2(dim(d + 8) * up, dim(d + 12) * up);
+    }
+  // down is a row-gi value on all four t lanes; the S fragment needs rows 2t, 2t+1.
+  Q.qm[0] = __shfl_sync(0xffffffffu, down, 8 * t);
+  Q.qm[1] = __shfl_sync(0xffffffffu, down, 8 * t + 4);
+}
+
 // tcgen05 history kernel (history_tc.cu); OSCAR_ERR_UNSUPPORTED for geometries it does
 // not cover (more than 32 query rows per KV head, other slot sizes).
 int history_tc_launch(const HistParams &P, int32_t num_tasks, cudaStream_t stream);
+
+// Opt-in history kernel for 9..24 query rows per KV head (MTP verify; history_mtp.cu):
+// four warps per KV head build every key and value operand once for all the head's rows.
+// OSCAR_ERR_UNSUPPORTED for other row counts.
+int history_mtp_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority);
 
 }  // namespace oscar
