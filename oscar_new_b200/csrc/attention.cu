@@ -1019,12 +1019,12 @@ static bool history_tc_enabled() {
   return v != nullptr && v[0] == '1';
 }
 
-// Opt-in switch for the shared-operand MTP kernel (9..24 rows per KV head), read at
-// every launch: it is parity-green but slower than history_attention_kernel on config 4
-// (its per-head barriers stall more than the shared operands save).
+// The shared-operand MTP kernel serves 9..24 rows per KV head (at most 4 KV heads) by
+// default; OSCAR_HISTORY_MTP=0 (read at every launch) sends those launches to
+// history_attention_kernel, for comparisons.
 static bool history_mtp_enabled() {
   const char *v = getenv("OSCAR_HISTORY_MTP");
-  return v != nullptr && v[0] == '1';
+  return v == nullptr || v[0] != '0';
 }
 
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {

@@ -173,9 +173,9 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
 // not cover (more than 32 query rows per KV head, other slot sizes).
 int history_tc_launch(const HistParams &P, int32_t num_tasks, cudaStream_t stream);
 
-// Opt-in history kernel for 9..24 query rows per KV head (MTP verify; history_mtp.cu):
-// four warps per KV head build every key and value operand once for all the head's rows.
-// OSCAR_ERR_UNSUPPORTED for other row counts.
+// History kernel for 9..24 query rows per KV head (MTP verify; history_mtp.cu): four
+// warps per KV head build every key and value operand once for all the head's rows.
+// OSCAR_ERR_UNSUPPORTED for other row counts and for more than 4 KV heads.
 int history_mtp_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority);
 
 }  // namespace oscar

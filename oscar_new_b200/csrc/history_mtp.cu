@@ -1,11 +1,7 @@
 // INT2 history attention for MTP verify and other launches with 9..24 query rows per
 // KV head (reference oscar_ascend/kernels.py:290-436, RAW=False; same partials, LSE and
-// split ranges as history_attention_kernel in attention.cu).  Opt-in (OSCAR_HISTORY_MTP=1):
-// parity-green, but on config 4 it takes 1.81 ms against 1.38 ms for the default kernel.
-// ncu (8-request config 4 case): 25 % fewer instructions per token-head than the default
-// kernel, yet issue active only 37 % with 2.7 barrier-stall cycles per issued instruction:
-// the four warps of a head meet twice per chunk, and the shared operands do not pay for
-// the waits.
+// split ranges as history_attention_kernel in attention.cu).  The default for those
+// launches (OSCAR_HISTORY_MTP=0 selects history_attention_kernel instead).
 //
 // history_attention_kernel gives every 8-row n-tile its own warp, and each of those warps
 // rebuilds the key and value operands of every token: at 24 rows per KV head (4 query
@@ -33,7 +29,9 @@ namespace {
 
 constexpr int kMtpChunk = 64;  // tokens per chunk: one 16-token m-tile per warp of a head
 constexpr int kMtpStages = 3;
-constexpr int kMtpHeadsPerCta = 2;
+// All KV heads of a token in one CTA (up to 4): a chunk is then one contiguous run and one
+// bulk copy; with fewer heads per CTA every token of the chunk needs its own copy.
+constexpr int kMtpHeadsPerCta = 4;
 constexpr int kMtpThreads = 128 * kMtpHeadsPerCta;
 
 // per-head shared-memory block (bytes)
@@ -41,7 +39,7 @@ template <int NT>
 struct MtpLayout {
   static constexpr int qfrag = 0;                       // [NT][16 k-steps][32 lanes] uint2
   static constexpr int qm = qfrag + NT * 16 * 32 * 8;   // [NT * 8] row scales
-  static constexpr int xmax = qm + 32 * 4;              // [4 warps][NT][4 t][2 r] chunk row maxima
+  static constexpr int xmax = qm + 32 * 4;              // [NT][4 t][2 r][4 warps] chunk row maxima
   static constexpr int pbuf = xmax + 4 * NT * 8 * 4;    // [4 k-steps][NT][32 lanes] uint2 P' fragments
   static constexpr int lz = pbuf + 4 * NT * 32 * 8;     // [4 warps][NT][4 t][2 r][2] l, sum p z
   static constexpr int bytes = (lz + 4 * NT * 8 * 2 * 4 + 127) / 128 * 128;
@@ -50,7 +48,7 @@ struct MtpLayout {
 OSCAR_DEVINL void head_bar(int hl) { asm volatile("bar.sync %0, 128;" ::"r"(1 + hl) : "memory"); }
 
 template <int NT>
-__global__ void __launch_bounds__(kMtpThreads, 2) history_mtp_kernel(HistParams P) {
+__global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   using L = MtpLayout<NT>;
   const oscar_geometry &g = P.geo;
@@ -267,12 +265,14 @@ __global__ void __launch_bounds__(kMtpThreads, 2) history_mtp_kernel(HistParams 
         }
       }
 #pragma unroll
-      for (int n = 0; n < NT; ++n)
+      for (int n = 0; n < NT; ++n) {
+        const float2 qmn = *reinterpret_cast<const float2 *>(qm_row + 8 * n + 2 * t);  // rows 2t, 2t+1
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float mul = (e < 2 ? lA.inv : lB.inv) * qm_row[8 * n + 2 * t + (e & 1)];
+          const float mul = (e < 2 ? lA.inv : lB.inv) * ((e & 1) ? qmn.y : qmn.x);
           lg[n][e] = ((e < 2) ? va : vb) ? sc[n][e] * mul : -INFINITY;
         }
+      }
     } else {
 #pragma unroll
       for (int n = 0; n < NT; ++n) lg[n][0] = lg[n][1] = lg[n][2] = lg[n][3] = -INFINITY;
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(kMtpThreads, 2) history_mtp_kernel(HistParams 
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        if (gi == 0) xmax[((w * NT + n) * 4 + t) * 2 + r] = mx;
+        if (gi == 0) xmax[((n * 4 + t) * 2 + r) * 4 + w] = mx;  // the head's 4 warps side by side
       }
     head_bar(hl);
     // Abort snapshot: every write of the word (a full-barrier timeout of this chunk, a
@@ -303,9 +303,8 @@ __global__ void __launch_bounds__(kMtpThreads, 2) history_mtp_kernel(HistParams 
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        float mx = xmax[((0 * NT + n) * 4 + t) * 2 + r];
-#pragma unroll
-        for (int w2 = 1; w2 < 4; ++w2) mx = fmaxf(mx, xmax[((w2 * NT + n) * 4 + t) * 2 + r]);
+        const float4 xw = *reinterpret_cast<const float4 *>(xmax + ((n * 4 + t) * 2 + r) * 4);
+        const float mx = fmaxf(fmaxf(xw.x, xw.y), fmaxf(xw.z, xw.w));
         mc[n][r] = mx;
         need_any |= mx > m_run[n][r] + kRescaleSlack || (m_run[n][r] == -INFINITY && mx > -INFINITY);
       }
@@ -439,7 +438,8 @@ __global__ void __launch_bounds__(kMtpThreads, 2) history_mtp_kernel(HistParams 
 template <int NT>
 int launch_mtp(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority) {
   const oscar_geometry &g = P.geo;
-  const int hpc = g.kv_heads % kMtpHeadsPerCta == 0 ? kMtpHeadsPerCta : 1;
+  if (g.kv_heads > kMtpHeadsPerCta) return OSCAR_ERR_UNSUPPORTED;
+  const int hpc = g.kv_heads;
   P.heads_per_cta = hpc;
   P.ntiles = NT;
   P.units = hpc * NT;

@@ -434,20 +434,22 @@ def test_decode_step_tcgen05_history_opt_in(cuda_lib, monkeypatch, name, seq, ql
     [
         ("mtp_verify", [900, 2049, 1400], [4, 4, 3], 24, 4, make_config(4, 128, 3), 8),
         ("skewed_balanced", [140, 9000, 333, 2, 1500], [4, 4, 1, 2, 4], 24, 4, make_config(4, 128, 3), 64),
-        ("wide_8heads", [1300, 2600], [4, 4], 32, 8, make_config(4, 128, 3), 8),
+        ("group4_16rows", [1300, 2600], [4, 4], 16, 4, make_config(4, 128, 3), 8),
         ("mid_2heads", [1100, 3100], [4, 3], 12, 2, make_config(4, 128, 3), 8),
     ],
 )
-def test_decode_step_mtp_kernel_opt_in(cuda_lib, monkeypatch, name, seq, qlen, hq, h, cfg, splits):
-    """The opt-in shared-operand MTP kernel (OSCAR_HISTORY_MTP=1: four warps per KV head,
-    16 or 24 rows) against the dense hybrid reference; its execution is asserted by name."""
-    monkeypatch.setenv("OSCAR_HISTORY_MTP", "1")
+@pytest.mark.parametrize("mtp_env,kernel", [("1", "history_mtp_kernel"), ("0", "history_attention_kernel")])
+def test_decode_step_mtp_kernel_choice(cuda_lib, monkeypatch, mtp_env, kernel, name, seq, qlen, hq, h, cfg, splits):
+    """16 and 24 rows per KV head: the shared-operand MTP kernel (the default; four warps
+    per KV head) and, with OSCAR_HISTORY_MTP=0, the per-row-tile kernel, both against the
+    dense hybrid reference; which kernel ran is asserted by name."""
+    monkeypatch.setenv("OSCAR_HISTORY_MTP", mtp_env)
     sc = Scenario(seq, qlen, hq=hq, h=h, cfg=cfg, seed=len(name))
     with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
         out = sc.run_step(splits).float().cpu()
         torch.cuda.synchronize()
     names = {e.name for e in prof.events()}
-    assert any("history_mtp_kernel" in nm for nm in names), names
+    assert any(kernel in nm for nm in names), names
     expect, _ = sc.expected()
     assert rel_err(out, expect) < 1e-2, rel_err(out, expect)
     torch.testing.assert_close(out, expect, atol=0.035, rtol=0.04)
