@@ -1,14 +1,16 @@
-// Exact percentile clip + INT2 quantise + pack of one D=256 vector per warp.
+// Exact percentile clip + INT2 quantise + pack of D=256 vectors, two per warp.
 //
-// Each lane owns dims [8*lane, 8*lane+8).  The arithmetic reproduces the reference
-// oracle bit for bit (tests/oracle.py:6-21 with kernels.py:104-137 byte order):
+// The arithmetic reproduces the reference oracle bit for bit (tests/oracle.py:6-21 with
+// kernels.py:104-137 byte order):
 //   thr   = torch.quantile(|x|, ratio) = lerp(asc[lo], asc[hi], w) as a CPU fused
 //           multiply-add (w < .5 ? fma(w, b-a, a) : fma(w-1, b-a, b)), or max|x|*factor
 //   x     = min(max(x, -thr), thr)
 //   zero  = fp16_rn(min x), scale = fp16_rn(max((max x - min x) / 3, 2^-14))
-//   code  = clamp(trunc((x - zero) / scale + 0.5), 0, 3), IEEE ops, no contraction
+//   code  = clamp(trunc((x - zero) / scale + 0.5), 0, 3), IEEE ops, no contraction; an
+//           infinite or NaN quotient (zero or scale beyond fp16) converts to INT_MIN on
+//           the reference's x86 host, i.e. code 0
 //   bytes = codes LSB-first, 4 per byte; then scale, zero as little-endian fp16.
-// The order statistics are found exactly by a bisection over the 15-bit magnitude
+// The order statistics are found exactly by counting passes over the 15-bit magnitude
 // keys of the (bf16-valued) inputs, with warp-wide integer reductions.
 #pragma once
 
@@ -16,91 +18,11 @@
 
 namespace oscar {
 
-// k-th largest (1-indexed) 15-bit key among the 256 keys of the warp.
-OSCAR_DEVINL uint32_t warp_kth_largest(const uint32_t (&key)[8], int k) {
-  uint32_t v = 0;
-#pragma unroll 1
-  for (int b = 14; b >= 0; --b) {
-    const uint32_t t = v | (1u << b);
-    uint32_t c = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) c += key[i] >= t ? 1u : 0u;
-    c = __reduce_add_sync(0xffffffffu, c);
-    if (c >= (uint32_t)k) v = t;
-  }
-  return v;
-}
-
-// Quantise the warp's vector x (fp32 copies of bf16 values) and write the 68-byte
-// packed vector at dst (only when `write`; the warp still participates otherwise).
-OSCAR_DEVINL void quantize_pack_warp(float (&x)[8], const oscar_clip &clip, uint8_t *dst, bool write) {
-  const int lane = threadIdx.x & 31;
-  if (clip.enabled) {
-    float thr;
-    if (clip.mode == 1) {
-      float m = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(x[i]));
-      thr = __fmul_rn(warp_max(m), clip.factor);
-    } else {
-      uint32_t key[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) key[i] = (__float_as_uint(x[i]) & 0x7fffffffu) >> 16;
-      const int k_hi = 256 - clip.asc_hi;  // rank of the larger interpolation point
-      const uint32_t hi_key = warp_kth_largest(key, k_hi);
-      uint32_t lo_key = hi_key;
-      if (clip.asc_lo != clip.asc_hi) {
-        uint32_t ge = 0, below = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          ge += key[i] >= hi_key ? 1u : 0u;
-          if (key[i] < hi_key) below = max(below, key[i]);
-        }
-        ge = __reduce_add_sync(0xffffffffu, ge);
-        below = __reduce_max_sync(0xffffffffu, below);
-        if (ge < (uint32_t)(k_hi + 1)) lo_key = below;
-      }
-      const float a = __uint_as_float(lo_key << 16);
-      const float b = __uint_as_float(hi_key << 16);
-      const float d = __fsub_rn(b, a);
-      thr = clip.weight < 0.5f ? __fmaf_rn(clip.weight, d, a) : __fmaf_rn(__fsub_rn(clip.weight, 1.0f), d, b);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = fminf(fmaxf(x[i], -thr), thr);
-  }
-  float lo = x[0], hi = x[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) {
-    lo = fminf(lo, x[i]);
-    hi = fmaxf(hi, x[i]);
-  }
-  lo = warp_min(lo);
-  hi = warp_max(hi);
-  const uint16_t zero_h = float_to_half_bits(lo);
-  const uint16_t scale_h = float_to_half_bits(fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 3.0f), 6.103515625e-05f));
-  const float zf = half_bits_to_float(zero_h);
-  const float sf = half_bits_to_float(scale_h);
-  uint32_t packed = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float q = __fadd_rn(__fdiv_rn(__fsub_rn(x[i], zf), sf), 0.5f);
-    // truncation toward zero as torch .to(int32) on the x86 host: NaN and values out of
-    // the int32 range give INT_MIN (code 0), where CUDA's conversion would saturate
-    int c = (q > -2147483904.f && q < 2147483648.f) ? (int)q : INT_MIN;
-    c = min(max(c, 0), 3);
-    packed |= (uint32_t)c << (2 * i);
-  }
-  if (write) {
-    reinterpret_cast<uint16_t *>(dst)[lane] = (uint16_t)packed;
-    if (lane == 0) *reinterpret_cast<uint32_t *>(dst + kDataBytes) = (uint32_t)scale_h | ((uint32_t)zero_h << 16);
-  }
-}
-
 // ----------------------------------------------------------------------------
 // Two vectors per warp, on the bf16 values as they are stored: lanes 0-15 quantise
 // vector A, lanes 16-31 vector B; lane l = lane & 15 owns dims [16l, 16l+16) as eight
-// bf16 pairs (element 2i in the low half of word i).  Same result as
-// quantize_pack_warp, bit for bit, computed with packed bf16x2 compares:
+// bf16 pairs (element 2i in the low half of word i), computed with packed bf16x2
+// compares:
 //  * order statistics: counts of magnitudes >= t, two per compare, added as exact small
 //    integers in bf16 (count_ge_bf16);
 //  * min / max of the clipped vector: min / max of the raw values, then clipped (the

@@ -7,7 +7,9 @@
 namespace oscar {
 
 // ----------------------------------------------------------------------------
-// standalone store: one warp per (token, head) row, K then V
+// standalone store: two (token, head) rows per warp, one per half-warp (the packed bf16
+// quantiser of quant.cuh), K then V; a half whose row is absent or not stored still
+// takes part in the reductions
 // ----------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) store_int2_kernel(const __nv_bfloat16 *__restrict__ krot,
                                                          const __nv_bfloat16 *__restrict__ vrot,
@@ -15,27 +17,26 @@ __global__ void __launch_bounds__(256) store_int2_kernel(const __nv_bfloat16 *__
                                                          const int64_t *__restrict__ slots,
                                                          const int32_t *__restrict__ counts,
                                                          oscar_geometry geo, oscar_clip kc, oscar_clip vc) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int64_t token = row / geo.kv_heads;
-  const int head = (int)(row % geo.kv_heads);
-  if (token >= counts[1]) return;
-  const int64_t slot = slots[token];
-  if (slot < 0) return;
-  uint8_t *dst = history + slot_byte_offset(slot, head, geo);
+  const int lane = threadIdx.x & 31, l = lane & 15;
+  const int64_t pair = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (2 * pair >= rows) return;  // warp-uniform
+  const int64_t row = 2 * pair + (lane >> 4);
+  bool live = row < rows;
+  uint8_t *dst = nullptr;
+  if (live) {
+    const int64_t token = row / geo.kv_heads;
+    const int head = (int)(row - token * geo.kv_heads);
+    const int64_t slot = token < counts[1] ? slots[token] : -1;
+    live = slot >= 0;
+    if (live) dst = history + slot_byte_offset(slot, head, geo);
+  }
+  const int64_t rr = row < rows ? row : 2 * pair;
 #pragma unroll 1
   for (int kv = 0; kv < 2; ++kv) {
-    const __nv_bfloat16 *src = (kv == 0 ? krot : vrot) + row * kDim + lane * 8;
-    const uint4 raw = *reinterpret_cast<const uint4 *>(src);
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    float x[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[2 * i] = bf16_bits_to_float(w[i] & 0xffffu);
-      x[2 * i + 1] = bf16_bits_to_float(w[i] >> 16);
-    }
-    quantize_pack_warp(x, kv == 0 ? kc : vc, dst + kv * geo.vector_bytes, true);
+    const uint4 *src = reinterpret_cast<const uint4 *>((kv == 0 ? krot : vrot) + rr * kDim + 16 * l);
+    const uint4 r0 = src[0], r1 = src[1];
+    const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    quantize_pack_half(w, kv == 0 ? kc : vc, live ? dst + kv * geo.vector_bytes : nullptr, live);
   }
 }
 
@@ -206,7 +207,7 @@ extern "C" int oscar_store_int2(const void *krot, const void *vrot, int64_t n, v
   if (!krot || !vrot || !history || !slots || !counts) return OSCAR_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(krot) | reinterpret_cast<uintptr_t>(vrot)) & 15) return OSCAR_ERR_INVALID;
   const int64_t rows = n * geo.kv_heads;
-  store_int2_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+  store_int2_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16 *>(krot), reinterpret_cast<const __nv_bfloat16 *>(vrot), rows,
       reinterpret_cast<uint8_t *>(history), slots, counts, geo, kclip, vclip);
   OSCAR_CHECK_LAUNCH();
