@@ -885,11 +885,16 @@ __global__ void __launch_bounds__(256) window_store_kernel(const __nv_bfloat16 *
   // Positions this step writes: sink positions in [prefix, min(seq, S)) and, for the
   // ring, each slot's latest writer, i.e. pos >= S with pos + C >= seq.  Same set as
   // the reference's per-slot latest-writer rule (kernels.py:576-582).
+  // Only those positions are visited (a prefill chunk of thousands of tokens writes at
+  // most sink + ring of them): sink [lo, min(seq, S)), ring [max(lo, S, seq - C), seq).
   const int lo = max(prefix, 0);
-  const int entries = (seq - lo) * g.kv_heads;
+  const int n_sink = max(0, min(seq, g.sink) - lo);
+  const int ring_lo = max(max(lo, g.sink), seq - g.ring);
+  const int n_ring = max(0, seq - ring_lo);
+  const int entries = (n_sink + n_ring) * g.kv_heads;
   for (int e = warp; e < entries; e += 8) {
-    const int pos = lo + e / g.kv_heads, head = e % g.kv_heads;
-    if (!(pos < g.sink || pos + g.ring >= seq)) continue;
+    const int k = e / g.kv_heads, head = e % g.kv_heads;
+    const int pos = k < n_sink ? lo + k : ring_lo + (k - n_sink);
     const int idx = pos < g.sink ? pos : g.sink + pos % g.ring;
     const int cur = qstart + pos - prefix;
     const uint4 kv0 = *reinterpret_cast<const uint4 *>(key + (int64_t)cur * ks0 + (int64_t)head * ks1 + lane * 8);

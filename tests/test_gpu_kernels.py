@@ -307,9 +307,11 @@ def test_prepare_tasks_copies_table_columns(cuda_lib):
     assert (dst[3:] == -1).all() and (dst[:, 17:] == -1).all()
 
 
-def test_store_windows_matches_oracle(cuda_lib):
+@pytest.mark.parametrize("seq,qlen", [([30, 70, 5], [20, 4, 5]), ([1500, 40, 700], [1200, 40, 3])])
+def test_store_windows_matches_oracle(cuda_lib, seq, qlen):
+    """Sink and ring slots (latest writer only), short and prefill-sized chunks."""
     cfg = make_config(sink=4, recent=16, mtp=3)
-    sc = Scenario([30, 70, 5], [20, 4, 5], hq=6, h=2, cfg=cfg, block_tokens=256, seed=5)
+    sc = Scenario(seq, qlen, hq=6, h=2, cfg=cfg, block_tokens=256, seed=5)
     q, k, v = sc.current()
     before = sc.window.cpu()
     kernels.store_windows(k, v, sc.window, sc.meta, sc.layout)
