@@ -210,9 +210,9 @@ constexpr int kJRows = kDim / kJCtas;  // 32 rows per CTA
 constexpr int kJThreads = 256;
 
 struct JacobiSmem {
-  double a[kJRows][kDim];
+  double a[kJRows][kDim];   // local rows of A at the start of a round
+  double nx[kJRows][kDim];  // local rows of A J (column-rotated), read by the partner rows' owners
   double u[kJRows][kDim];
-  double tmp[kJRows][kDim];
   double cs[kDim / 2][2];
   double diag[kDim];
   double stat[2];
@@ -262,68 +262,56 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
   int sweeps_done = 0;
   bool finite = true;
   for (int sweep = 0; sweep < max_sweeps; ++sweep) {
+    // Two cluster barriers per round: the column-rotated rows go to a second buffer (nx),
+    // so the partner-row reads of step 3 never race with a write, and each CTA computes
+    // the rotation parameters of all pairs itself from the current rows.
     for (int r = 0; r < kDim - 1; ++r) {
-      // (1) rotation parameters of the pairs whose p-row is local, pushed to all CTAs
+      // (1) rotation parameters of all pairs, from the (possibly remote) current rows
       if (tid < kDim / 2) {
         int p, q;
         round_pair(tid, r, p, q);
-        if (p / kJRows == rank) {
-          const double app = S.a[p - row0][p];
-          const double apq = S.a[p - row0][q];
-          const JacobiSmem *owner_q = cluster.map_shared_rank(&S, q / kJRows);
-          const double aqq = owner_q->a[q % kJRows][q];
-          const double delta = (aqq - app) * 0.5;
-          const double sgn = delta >= 0.0 ? 1.0 : -1.0;
-          double tang = sgn * apq / fmax(fabs(delta) + sqrt(delta * delta + apq * apq), 1e-30);
-          if (!(fabs(apq) > 1e-8 * (fabs(app) + fabs(aqq)) + 1e-20)) tang = 0.0;
-          const double cs = 1.0 / sqrt(1.0 + tang * tang);
-          const double sn = tang * cs;
-          for (int dst = 0; dst < kJCtas; ++dst) {
-            JacobiSmem *o = cluster.map_shared_rank(&S, dst);
-            o->cs[tid][0] = cs;
-            o->cs[tid][1] = sn;
-          }
-        }
+        const JacobiSmem *owner_p = cluster.map_shared_rank(&S, p / kJRows);
+        const JacobiSmem *owner_q = cluster.map_shared_rank(&S, q / kJRows);
+        const double app = owner_p->a[p % kJRows][p];
+        const double apq = owner_p->a[p % kJRows][q];
+        const double aqq = owner_q->a[q % kJRows][q];
+        const double delta = (aqq - app) * 0.5;
+        const double sgn = delta >= 0.0 ? 1.0 : -1.0;
+        double tang = sgn * apq / fmax(fabs(delta) + sqrt(delta * delta + apq * apq), 1e-30);
+        if (!(fabs(apq) > 1e-8 * (fabs(app) + fabs(aqq)) + 1e-20)) tang = 0.0;
+        const double cs = 1.0 / sqrt(1.0 + tang * tang);
+        S.cs[tid][0] = cs;
+        S.cs[tid][1] = tang * cs;
       }
-      cluster.sync();
-      // (2) column rotations of the local rows of A and U
+      __syncthreads();
+      // (2) column rotations of the local rows: nx = A J; U = U J in place
       for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
         const int lr = e / (kDim / 2), j = e % (kDim / 2);
         int p, q;
         round_pair(j, r, p, q);
         const double c = S.cs[j][0], s = S.cs[j][1];
         const double ap = S.a[lr][p], aq = S.a[lr][q];
-        S.a[lr][p] = ap * c - aq * s;
-        S.a[lr][q] = ap * s + aq * c;
+        S.nx[lr][p] = ap * c - aq * s;
+        S.nx[lr][q] = ap * s + aq * c;
         const double up = S.u[lr][p], uq = S.u[lr][q];
         S.u[lr][p] = up * c - uq * s;
         S.u[lr][q] = up * s + uq * c;
       }
       cluster.sync();
-      // (3) fetch each local row's partner row (possibly remote), then (4) row rotations
-      // 16-byte loads: a local row is 256 doubles = 128 double2; the 16 remote loads of
-      // a thread are independent and unrolled so that they are in flight together
+      // (3) row rotations: each local row x of J^T (A J) from its own nx row and its
+      // partner's nx row y, read from y's owner (16-byte loads, independent and unrolled
+      // so that they are in flight together)
 #pragma unroll
       for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
         const int lr = e / (kDim / 2), c2 = e % (kDim / 2);
         const int x = row0 + lr;
-        int y;
-        if (x == kDim - 1) y = r;
-        else if (x == r) y = kDim - 1;
-        else y = mod_dm1(mod_dm1(2 * r - x));
-        const JacobiSmem *own = cluster.map_shared_rank(&S, y / kJRows);
-        reinterpret_cast<double2 *>(S.tmp[lr])[c2] = reinterpret_cast<const double2 *>(own->a[y % kJRows])[c2];
-      }
-      cluster.sync();
-      for (int e = tid; e < kJRows * kDim; e += kJThreads) {
-        const int lr = e / kDim, col = e % kDim;
-        const int x = row0 + lr;
-        int j, isp;
+        int y, j, isp;
         if (x == kDim - 1) {
-          j = 0, isp = 1;
+          y = r, j = 0, isp = 1;
         } else if (x == r) {
-          j = 0, isp = 0;
+          y = kDim - 1, j = 0, isp = 0;
         } else {
+          y = mod_dm1(mod_dm1(2 * r - x));
           const int jp = mod_dm1(x - r);  // x = (r + jp) mod (D-1)
           if (jp >= 1 && jp < kDim / 2) {
             j = jp, isp = 1;
@@ -331,9 +319,14 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
             j = mod_dm1(r - x), isp = 0;  // x = (r - j) mod (D-1)
           }
         }
+        const JacobiSmem *own = cluster.map_shared_rank(&S, y / kJRows);
+        const double2 by = reinterpret_cast<const double2 *>(own->nx[y % kJRows])[c2];
+        const double2 bx = reinterpret_cast<const double2 *>(S.nx[lr])[c2];
         const double c = S.cs[j][0], s = S.cs[j][1];
-        const double bx = S.a[lr][col], by = S.tmp[lr][col];
-        S.a[lr][col] = isp ? (c * bx - s * by) : (s * by + c * bx);
+        double2 o;
+        o.x = isp ? (c * bx.x - s * by.x) : (s * by.x + c * bx.x);
+        o.y = isp ? (c * bx.y - s * by.y) : (s * by.y + c * bx.y);
+        reinterpret_cast<double2 *>(S.a[lr])[c2] = o;
       }
       cluster.sync();
     }
@@ -379,11 +372,11 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
     }
   }
   // eigenvalues: gather the diagonal, rank ascending (ties by index)
-  if (tid < kJRows) S.tmp[0][row0 + tid] = S.a[tid][row0 + tid];
+  if (tid < kJRows) S.nx[0][row0 + tid] = S.a[tid][row0 + tid];
   cluster.sync();
   for (int i = tid; i < kDim; i += kJThreads) {
     const JacobiSmem *own = cluster.map_shared_rank(&S, i / kJRows);
-    S.diag[i] = own->tmp[0][i];
+    S.diag[i] = own->nx[0][i];
   }
   cluster.sync();
   for (int i = tid; i < kDim; i += kJThreads) {
@@ -400,13 +393,13 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
   // sorted U rows (local), Hadamard butterfly, bit-reversed placement, / sqrt(256)
   for (int e = tid; e < kJRows * kDim; e += kJThreads) {
     const int lr = e / kDim, i = e % kDim;
-    S.tmp[lr][rank_of[i]] = S.u[lr][i];
+    S.nx[lr][rank_of[i]] = S.u[lr][i];
   }
   __syncthreads();
   for (int lr = warp; lr < kJRows; lr += 8) {
     double v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = S.tmp[lr][8 * lane + e];
+    for (int e = 0; e < 8; ++e) v[e] = S.nx[lr][8 * lane + e];
 #pragma unroll
     for (int bit = 0; bit < 3; ++bit) {
       double nv[8];
