@@ -182,6 +182,13 @@ class CalibrationSession:
         if eigensolver is None:
             eigensolver = self.ops.calibrated_rotations
         rotations, eigenvalues, convergence = eigensolver(covariances, max_sweeps=max_sweeps)
+        # the reference's per-matrix check, allclose(R^T R, I, atol=rtol=0.005) and finite
+        # entries, batched where the rotations are (one launch instead of 2 x layers host
+        # matrix products)
+        gram = torch.matmul(rotations.transpose(-1, -2), rotations)
+        eye = torch.eye(DIM, dtype=rotations.dtype, device=rotations.device)
+        valid = (torch.isfinite(rotations).flatten(1).all(1)
+                 & ((gram - eye).abs() <= 0.005 + 0.005 * eye).flatten(1).all(1)).cpu()
         rotations_cpu, eigenvalues_cpu = rotations.cpu(), eigenvalues.cpu()
         output = Path(output_dir)
         output.mkdir(parents=True, exist_ok=True)
@@ -204,9 +211,7 @@ class CalibrationSession:
             }
             for number, index in enumerate(layers):
                 matrix = rotations_cpu[number * 2 + offset]
-                identity = torch.eye(DIM, dtype=matrix.dtype)
-                if not torch.isfinite(matrix).all() or not torch.allclose(matrix.T @ matrix, identity, atol=0.005,
-                                                                          rtol=0.005):
+                if not bool(valid[number * 2 + offset]):
                     raise RuntimeError(f"Generated {kind} rotation for layer {index} failed validation")
                 result["layers"][index] = {"layer_id": index, "rotation": matrix,
                                            "eigenvalues": eigenvalues_cpu[number * 2 + offset]}

@@ -196,3 +196,22 @@ def test_two_rank_gloo_sharding_matches_single_process(tmp_path, shard):
     ck = torch.load(tmp_path / shard / "k_rotation.pt", weights_only=True)
     assert ck["calibration"]["world_size"] == 2 and ck["calibration"]["shard"] == shard
     assert not (tmp_path / shard / "k_rotation.pt.tmp").exists()
+
+
+def test_finish_rejects_a_rotation_that_is_not_orthogonal(tmp_path):
+    """The publication check (R^T R within 0.005 of I, finite entries) stops finish
+    before the failing kind's checkpoint is written (kinds are published in the order
+    k, v, as in the reference); the message names the kind and layer."""
+    data = activations([3, 7], 300, 1, 2, seed=6)
+    s = CalibrationSession([3, 7], 10**9, "cpu", num_kv_heads=1, group_size=2, ops=CpuOps)
+    run_passes(s, data, chunk=300)
+
+    def bad_solver(covariances, max_sweeps=12):
+        rotations, eigenvalues, info = eigh_rotations(covariances, max_sweeps=max_sweeps)
+        rotations = rotations.clone()
+        rotations[3] *= 1.01  # layer 7, value rotation: R^T R = 1.0201 I
+        return rotations, eigenvalues, info
+
+    with pytest.raises(RuntimeError, match="v rotation for layer 7 failed validation"):
+        s.finish(tmp_path, {"model_fingerprint": "x"}, 12, eigensolver=bad_solver)
+    assert not (tmp_path / "v_rotation.pt").exists() and not list(tmp_path.glob("*.tmp"))
