@@ -201,7 +201,8 @@ int oscar_accumulate_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int6
                           const float *weights, float *cov, void *stream);
 
 /* w[t] = max(k_t C k_t^T, 0) for the n*h rows of bf16 K, and *total += sum w.
- * Reference :73-126 (generalised to any number of heads). */
+ * K 16-byte aligned with ks0, ks1 multiples of 8 elements (else OSCAR_ERR_INVALID);
+ * C fp32, 16-byte aligned.  Reference :73-126 (generalised to any number of heads). */
 int oscar_sst_weights(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1,
                       const float *q_cov, float *weights, float *total, void *stream);
 

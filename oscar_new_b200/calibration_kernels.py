@@ -73,8 +73,8 @@ def sst_weights_per_head(key: torch.Tensor, q_covariances: torch.Tensor, totals:
     n, h, d = key.shape
     if q_covariances.shape != (h, 256, 256) or totals.numel() != h or not totals.is_contiguous():
         raise ValueError("one covariance and one total per head")
-    if key.dtype != torch.bfloat16:
-        key = key.to(torch.bfloat16)
+    if key.dtype != torch.bfloat16 or key.stride(2) != 1 or key.stride(0) % 8 or key.stride(1) % 8 or key.data_ptr() % 16:
+        key = key.to(torch.bfloat16).contiguous()
     c = q_covariances.float().contiguous()
     weights = torch.empty(n * h, device=key.device, dtype=torch.float32)
     _lib.call("oscar_sst_weights_per_head", key.data_ptr(), n, h, key.stride(0), key.stride(1), c.data_ptr(),
@@ -87,8 +87,8 @@ def sst_weights(key: torch.Tensor, q_covariance: torch.Tensor, total_weight: tor
     (reference calibration_kernels.py:109-126; any number of KV heads)."""
     _cuda(key, q_covariance, total_weight)
     n, h, d = key.shape
-    if key.dtype != torch.bfloat16:
-        key = key.to(torch.bfloat16)
+    if key.dtype != torch.bfloat16 or key.stride(2) != 1 or key.stride(0) % 8 or key.stride(1) % 8 or key.data_ptr() % 16:
+        key = key.to(torch.bfloat16).contiguous()
     c = q_covariance.float().contiguous()
     weights = torch.empty(n * h, device=key.device, dtype=torch.float32)
     _lib.call("oscar_sst_weights", key.data_ptr(), n, h, key.stride(0), key.stride(1), c.data_ptr(),

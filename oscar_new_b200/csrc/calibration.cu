@@ -127,71 +127,134 @@ __global__ void __launch_bounds__(256) gram_kernel(const __nv_bfloat16 *__restri
 }
 
 // ----------------------------------------------------------------------------
-// SST weights: w_t = max(k_t C k_t^T, 0); total += sum w.  CTA = 32 rows; thread j
-// owns column j of y = K C, fp32 FMAs (reference keeps this product in fp32).
+// SST weights on tensor cores: w_r = max(k_r C k_r^T, 0) for 64 rows per CTA.  C (fp32)
+// is split exactly into three bf16 parts (hi + mid + lo carry its 24 significand bits),
+// so each bf16 MMA product with the bf16 key is exact and accumulates in fp32, as the
+// fp32 FMA form does.  C is taken in 64-row blocks: Y = K C_blk^T (C's rows as B's
+// columns; k C k^T is a scalar, so C or C^T give the same sum), then
+// w_r += sum_j Y[r][j] k_r[j].  The per-row partials of each (block, warp column) go to
+// their own shared-memory slot and are added in a fixed order.
 // ----------------------------------------------------------------------------
-// per_head = 0: rows (token, head) of all heads against one C and one total;
-// per_head = 1: blockIdx.y = head, rows are that head's tokens against C[head], total[head].
-__global__ void __launch_bounds__(256) sst_kernel(const __nv_bfloat16 *__restrict__ k, int64_t n, int32_t h,
-                                                  int64_t ks0, int64_t ks1, const float *__restrict__ c_base,
-                                                  float *__restrict__ w, float *__restrict__ total_base,
-                                                  int32_t per_head) {
-  __shared__ __align__(16) float sk[kDim][32];  // [i][row]
-  __shared__ float red[8][32];
+constexpr int kSstRows = 64;
+constexpr int kSstTileBytes = kSstRows * kDim * 2;          // 64 rows of 256 bf16
+constexpr int kSstSmem = 4 * kSstTileBytes + 8 * kSstRows * 4;  // K, 3 parts of C, partials
+
+// byte offset of 16-byte chunk c of row r in a [rows][256] bf16 tile (XOR swizzle, so the
+// eight rows of an ldmatrix land on distinct banks)
+OSCAR_DEVINL uint32_t sst_swz(int r, int c) { return (uint32_t)(r * 512 + ((c ^ (r & 7)) << 4)); }
+
+__global__ void __launch_bounds__(256, 1) sst_tc_kernel(const __nv_bfloat16 *__restrict__ k, int64_t n, int32_t h,
+                                                        int64_t ks0, int64_t ks1, const float *__restrict__ c_base,
+                                                        float *__restrict__ w, float *__restrict__ total_base,
+                                                        int32_t per_head) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *ktile = smem;
+  uint8_t *parts = smem + kSstTileBytes;  // [3][64 rows of C][256]
+  float *wpart = reinterpret_cast<float *>(smem + 4 * kSstTileBytes);  // [4 blocks][2 halves][64 rows]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gi = lane >> 2, t = lane & 3;
   const int head = per_head ? (int)blockIdx.y : 0;
   const float *c = c_base + (size_t)head * kDim * kDim;
-  float *total = total_base + head;
   const int64_t rows = per_head ? n : n * h;
-  const int64_t r0 = (int64_t)blockIdx.x * 32;
+  const int64_t r0 = (int64_t)blockIdx.x * kSstRows;
   auto out_index = [&](int64_t row) { return per_head ? row * h + head : row; };
-  for (int e = tid; e < 32 * kDim; e += 256) {
-    const int r = e / kDim, i = e % kDim;
+  // key rows (zero beyond the last row)
+  for (int e = tid; e < kSstRows * 32; e += 256) {
+    const int r = e >> 5, ch = e & 31;
     const int64_t row = r0 + r;
-    float v = 0.f;
+    uint4 v = make_uint4(0, 0, 0, 0);
     if (row < rows) {
       const __nv_bfloat16 *src = per_head ? k + row * ks0 + head * ks1 : k + (row / h) * ks0 + (row % h) * ks1;
-      v = bf16_bits_to_float(reinterpret_cast<const uint16_t *>(src)[i]);
+      v = reinterpret_cast<const uint4 *>(src)[ch];
     }
-    sk[i][r] = v;
+    *reinterpret_cast<uint4 *>(ktile + sst_swz(r, ch)) = v;
+  }
+  const int wm = warp & 3, wn = warp >> 2;  // rows 16 wm.., columns 32 wn.. of a block
+  const uint32_t kbase = smem_u32(ktile), pbase = smem_u32(parts);
+#pragma unroll 1
+  for (int nb = 0; nb < kDim / kSstRows; ++nb) {
+    __syncthreads();  // the previous block's parts are no longer read
+    for (int e = tid; e < kSstRows * 32; e += 256) {
+      const int jr = e >> 5, ch = e & 31;
+      const float4 *src = reinterpret_cast<const float4 *>(c + (size_t)(nb * kSstRows + jr) * kDim + ch * 8);
+      const float4 f0 = src[0], f1 = src[1];
+      const float x[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+      uint32_t hw[4], mw[4], lw[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float hv[2], mv[2], lv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float v = x[2 * q + u];
+          hv[u] = round_bf16(v);
+          const float r1 = v - hv[u];
+          mv[u] = round_bf16(r1);
+          lv[u] = round_bf16(r1 - mv[u]);
+        }
+        hw[q] = pack_bf162(hv[0], hv[1]);
+        mw[q] = pack_bf162(mv[0], mv[1]);
+        lw[q] = pack_bf162(lv[0], lv[1]);
+      }
+      const uint32_t off = sst_swz(jr, ch);
+      *reinterpret_cast<uint4 *>(parts + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4 *>(parts + kSstTileBytes + off) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+      *reinterpret_cast<uint4 *>(parts + 2 * kSstTileBytes + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    __syncthreads();
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll 4
+    for (int ks = 0; ks < kDim / 16; ++ks) {
+      uint32_t a[4];
+      ldmatrix_x4(a, kbase + sst_swz(16 * wm + (lane & 15), 2 * ks + (lane >> 4)));
+#pragma unroll
+      for (int part = 0; part < 3; ++part) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t b[4];
+          const int nrow = 32 * wn + 16 * hf + ((lane >> 4) << 3) + (lane & 7);
+          ldmatrix_x4(b, pbase + part * kSstTileBytes + sst_swz(nrow, 2 * ks + ((lane >> 3) & 1)));
+          mma_bf16_16816(acc[2 * hf], a[0], a[1], a[2], a[3], b[0], b[1]);
+          mma_bf16_16816(acc[2 * hf + 1], a[0], a[1], a[2], a[3], b[2], b[3]);
+        }
+      }
+    }
+    // partial w of rows 16 wm + gi (+8) over this warp's 32 columns
+    float s0 = 0.f, s1 = 0.f;
+    const int ra = 16 * wm + gi, rb = ra + 8;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = nb * kSstRows + 32 * wn + 8 * nt + 2 * t;
+      const uint32_t ka = *reinterpret_cast<const uint32_t *>(ktile + sst_swz(ra, col >> 3) + (col & 7) * 2);
+      const uint32_t kb = *reinterpret_cast<const uint32_t *>(ktile + sst_swz(rb, col >> 3) + (col & 7) * 2);
+      s0 = fmaf(acc[nt][0], bf16_bits_to_float(ka & 0xffffu), s0);
+      s0 = fmaf(acc[nt][1], bf16_bits_to_float(ka >> 16), s0);
+      s1 = fmaf(acc[nt][2], bf16_bits_to_float(kb & 0xffffu), s1);
+      s1 = fmaf(acc[nt][3], bf16_bits_to_float(kb >> 16), s1);
+    }
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    if (t == 0) {
+      wpart[(nb * 2 + wn) * kSstRows + ra] = s0;
+      wpart[(nb * 2 + wn) * kSstRows + rb] = s1;
+    }
   }
   __syncthreads();
-  const int j = tid;
-  float y[32];
-#pragma unroll
-  for (int r = 0; r < 32; ++r) y[r] = 0.f;
-  for (int i = 0; i < kDim; ++i) {
-    const float cij = c[i * kDim + j];
-    const float4 *kv = reinterpret_cast<const float4 *>(&sk[i][0]);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 kk = kv[q];
-      y[4 * q] = fmaf(kk.x, cij, y[4 * q]);
-      y[4 * q + 1] = fmaf(kk.y, cij, y[4 * q + 1]);
-      y[4 * q + 2] = fmaf(kk.z, cij, y[4 * q + 2]);
-      y[4 * q + 3] = fmaf(kk.w, cij, y[4 * q + 3]);
-    }
-  }
-  // w_r = sum_j y[r][j] * k[r][j]
-#pragma unroll
-  for (int r = 0; r < 32; ++r) {
-    float v = y[r] * sk[j][r];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[warp][r] = v;
-  }
-  __syncthreads();
-  if (warp == 0) {
+  if (warp < 2) {
+    const int r = tid;  // 0..63
     float v = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) v += red[q][lane];
+    for (int q = 0; q < 8; ++q) v += wpart[q * kSstRows + r];
     v = fmaxf(v, 0.f);
-    const bool ok = r0 + lane < rows;
-    if (ok) w[out_index(r0 + lane)] = v;
-    float s = ok ? v : 0.f;
+    const bool ok = r0 + r < rows;
+    if (ok) w[out_index(r0 + r)] = v;
+    float sum = ok ? v : 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) atomicAdd(total, s);
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) atomicAdd(total_base + head, sum);
   }
 }
 
@@ -474,9 +537,10 @@ extern "C" int oscar_sst_weights(const void *key, int64_t n, int32_t h, int64_t 
                                  float *weights, float *total, void *stream) {
   if (n < 0 || h <= 0 || !q_cov || !weights || !total) return OSCAR_ERR_INVALID;
   if (n == 0) return OSCAR_OK;
-  if (!key) return OSCAR_ERR_INVALID;
+  if (!key || (reinterpret_cast<uintptr_t>(key) & 15) || ks0 % 8 || ks1 % 8) return OSCAR_ERR_INVALID;
   const int64_t rows = n * h;
-  sst_kernel<<<(unsigned)((rows + 31) / 32), 256, 0, (cudaStream_t)stream>>>(
+  if (!ensure_dynamic_smem<sst_tc_kernel>(kSstSmem)) return OSCAR_ERR_LAUNCH;
+  sst_tc_kernel<<<(unsigned)((rows + kSstRows - 1) / kSstRows), 256, kSstSmem, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16 *>(key), n, h, ks0, ks1, q_cov, weights, total, 0);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
@@ -486,10 +550,11 @@ extern "C" int oscar_sst_weights_per_head(const void *key, int64_t n, int32_t h,
                                           const float *q_covs, float *weights, float *totals, void *stream) {
   if (n < 0 || h <= 0 || !q_covs || !weights || !totals) return OSCAR_ERR_INVALID;
   if (n == 0) return OSCAR_OK;
-  if (!key) return OSCAR_ERR_INVALID;
-  dim3 grid((unsigned)((n + 31) / 32), (unsigned)h);
-  sst_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16 *>(key), n, h, ks0, ks1,
-                                                     q_covs, weights, totals, 1);
+  if (!key || (reinterpret_cast<uintptr_t>(key) & 15) || ks0 % 8 || ks1 % 8) return OSCAR_ERR_INVALID;
+  if (!ensure_dynamic_smem<sst_tc_kernel>(kSstSmem)) return OSCAR_ERR_LAUNCH;
+  dim3 grid((unsigned)((n + kSstRows - 1) / kSstRows), (unsigned)h);
+  sst_tc_kernel<<<grid, 256, kSstSmem, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16 *>(key), n, h,
+                                                               ks0, ks1, q_covs, weights, totals, 1);
   OSCAR_CHECK_LAUNCH();
   return OSCAR_OK;
 }

@@ -588,6 +588,30 @@ def test_streamed_covariances_against_fp64(cuda_lib):
     torch.testing.assert_close(got, expect_v, atol=2e-4, rtol=2e-4)
 
 
+def test_sst_weights_match_fp64(cuda_lib):
+    """w = max(k C k^T, 0) per row and the weight totals against fp64: per-head and
+    shared covariances (outlier channels), 150 tokens (not a multiple of the 64-row
+    tile), a strided key view."""
+    torch.manual_seed(31)
+    n, h = 150, 4
+    k = torch.randn(n, 2 * h, 256).bfloat16()[:, ::2]
+    x = torch.randn(h, 600, 256)
+    x[..., :8] *= 20
+    covs = x.transpose(-1, -2) @ x / 600
+    kd = k.double()
+    expect = torch.einsum("nhi,hij,nhj->nh", kd, covs.double(), kd).clamp_min(0)
+    totals = torch.zeros(h, device=DEV)
+    w = ck.sst_weights_per_head(k.to(DEV), covs.to(DEV), totals)
+    scale = float(expect.abs().max())
+    torch.testing.assert_close(w.cpu().double().view(n, h), expect, rtol=1e-5, atol=1e-6 * scale)
+    torch.testing.assert_close(totals.cpu().double(), expect.sum(0), rtol=1e-5, atol=0.0)
+    total = torch.zeros((), device=DEV)
+    w1 = ck.sst_weights(k.to(DEV), covs[1].to(DEV), total)
+    expect1 = torch.einsum("nhi,ij,nhj->nh", kd, covs[1].double(), kd).clamp_min(0).reshape(-1)
+    torch.testing.assert_close(w1.cpu().double(), expect1, rtol=1e-5, atol=1e-6 * float(expect1.max()))
+    torch.testing.assert_close(total.cpu().double(), expect1.sum(), rtol=1e-5, atol=0.0)
+
+
 def test_device_eigensolver_reconstructs_and_matches_eigvalsh(cuda_lib):
     """Reference tests/test_npu_calibration.py:39-57 plus the project targets
     (eigenvalues rel 1e-4, ||R^T R - I|| < 1e-5)."""
