@@ -270,7 +270,8 @@ __global__ void normalize_kernel(const float *__restrict__ x, int64_t numel, con
 // ----------------------------------------------------------------------------
 constexpr int kJCtas = 8;
 constexpr int kJRows = kDim / kJCtas;  // 32 rows per CTA
-constexpr int kJThreads = 256;
+constexpr int kJThreads = 512;  // 16 warps: a round is latency-bound (remote rows, barriers)
+constexpr int kJWarps = kJThreads / 32;
 
 struct JacobiSmem {
   double a[kJRows][kDim];   // local rows of A at the start of a round
@@ -305,8 +306,8 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
                                                              float *__restrict__ evals, float *__restrict__ info) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   JacobiSmem &S = *reinterpret_cast<JacobiSmem *>(smem_raw);
-  __shared__ double wo[8], wd[8];
-  __shared__ int wf[8];
+  __shared__ double wo[kJWarps], wd[kJWarps];
+  __shared__ int wf[kJWarps];
   __shared__ int rank_of[kDim];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -416,7 +417,7 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
       if (tid == 0) {
         double o = 0.0, d = 0.0;
         int f = 1;
-        for (int q = 0; q < 8; ++q) o = fmax(o, wo[q]), d = fmax(d, wd[q]), f &= wf[q];
+        for (int q = 0; q < kJWarps; ++q) o = fmax(o, wo[q]), d = fmax(d, wd[q]), f &= wf[q];
         S.stat[0] = o, S.stat[1] = d, S.flag[0] = f;
       }
       cluster.sync();
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
     S.nx[lr][rank_of[i]] = S.u[lr][i];
   }
   __syncthreads();
-  for (int lr = warp; lr < kJRows; lr += 8) {
+  for (int lr = warp; lr < kJRows; lr += kJWarps) {
     double v[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = S.nx[lr][8 * lane + e];
