@@ -896,6 +896,30 @@ def profile_only(what):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
+    if what == "calibration":
+        from oscar_new_b200.calibration_worker import CalibrationSession
+
+        gen = torch.Generator(device=device).manual_seed(505)
+        layers, segments, tokens = 4, 4, 1024
+        data = {}
+        for layer in range(layers):
+            for seg in range(segments):
+                q = torch.randn(tokens, H * G, D, device=device, generator=gen)
+                k = torch.randn(tokens, H, D, device=device, generator=gen)
+                v = torch.randn(tokens, H, D, device=device, generator=gen)
+                for x in (q, k, v):
+                    x[..., :8] *= 20
+                data[(layer, seg)] = (q.bfloat16(), k.bfloat16(), v.bfloat16())
+        s = CalibrationSession(range(layers), 10**9, device, H, G, shard="tokens", group=None)
+        for phase in (1, 2):
+            for (layer, _), (q, k, v) in data.items():
+                s.observe(layer, q.view(tokens, -1), k.view(tokens, -1), v.view(tokens, -1), tokens)
+            if phase == 1:
+                s.second_pass()
+        s.finish(tempfile.mkdtemp(prefix="oscar_calib_"), {"model_fingerprint": "profile"}, 12)
+        torch.cuda.synchronize(device)
+        print("profile run done: calibration job (4 layers x 4 segments x 1024 tokens)")
+        return
     if what == "mtp-verify":
         from oscar_new_b200.config import decode_split_cap
 
@@ -946,7 +970,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
-    ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store", "mtp-verify"], default=None,
+    ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store", "mtp-verify", "calibration"],
+                    default=None,
                     help="build the state, run 4 launches of the kernel (or 4 layer steps) and exit")
     ap.add_argument("--workload", choices=["decode", "rotate-store", "mtp-verify", "calibration"], default="decode",
                     help="decode: config 3 (the headline); rotate-store: config 2; mtp-verify: config 4; "
