@@ -86,24 +86,6 @@ OSCAR_DEVINL void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-OSCAR_DEVINL void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-OSCAR_DEVINL void mma_u8s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                 uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 // Transpose an 8x8 b16 matrix held one 32-bit pair per lane (row = lane/4).
 OSCAR_DEVINL uint32_t movmatrix_trans(uint32_t x) {
   uint32_t r;
@@ -200,20 +182,6 @@ OSCAR_DEVINL void bulk_copy_g2s(uint32_t smem_dst, const void *gsrc, uint32_t by
           smem_dst),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
-}
-
-// ----------------------------------------------------------------------------
-// warp reductions
-// ----------------------------------------------------------------------------
-OSCAR_DEVINL float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-OSCAR_DEVINL float warp_min(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
 }
 
 // ----------------------------------------------------------------------------
