@@ -1,5 +1,6 @@
 """The C-ABI library loads on a CPU host and exports every symbol the header declares."""
 
+import ctypes
 import re
 from pathlib import Path
 
@@ -34,3 +35,18 @@ def test_invalid_arguments_are_rejected_without_launch():
     assert handle.oscar_store_int2(None, None, 4, None, None, None, geo, clip, clip, None) == 1
     assert handle.oscar_jacobi_rotations(None, 1, 0, 1e-6, None, None, None, None) == 1
     assert handle.oscar_rotate(None, 0, 1, 0, 0, 1, None, 0, 0, None, None) == 1
+
+
+def test_sst_weights_reject_keys_that_are_not_16_byte_rows():
+    """The SST entry points read key rows as 16-byte vectors: a key pointer off a 16-byte
+    boundary or strides that are not multiples of 8 elements are refused before any
+    device work (the pointers here are host placeholders and are never dereferenced)."""
+    handle = _lib.lib()
+    buf = (ctypes.c_char * 256)()
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    ok_ptr, off_ptr = base, base + 2
+    for fn in (handle.oscar_sst_weights, handle.oscar_sst_weights_per_head):
+        assert fn(off_ptr, 1, 1, 256, 256, ok_ptr, ok_ptr, ok_ptr, None) == 1
+        assert fn(ok_ptr, 1, 1, 260, 256, ok_ptr, ok_ptr, ok_ptr, None) == 1
+        assert fn(ok_ptr, 1, 1, 256, 260, ok_ptr, ok_ptr, ok_ptr, None) == 1
+        assert fn(ok_ptr, 0, 1, 260, 260, ok_ptr, ok_ptr, ok_ptr, None) == 0  # nothing to do
