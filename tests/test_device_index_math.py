@@ -1,0 +1,138 @@
+"""Index and bit arithmetic of the device kernels, restated on the CPU.
+
+The device code itself runs in the GPU tests; these tests pin the small exact
+arithmetic those kernels rely on, over every case rather than a sample:
+  * the history kernels' key operands (history_common.cuh `key_lut` and the PRMT
+    selectors `x * 0x11 + 0x40404040`) fetch exactly the reference's bf16 key levels,
+    for every byte of four 2-bit codes;
+  * the packed quantiser's counts (quant.cuh `count_ge_bf16`) stay exact small integers
+    in bf16 and read back from the low 7 bits of 128 + n;
+  * the MTP kernel's value byte lanes (history_mtp.cu) split the 256 dims among the four
+    warps of a head and extract the codes the reference's unpack assigns to those dims;
+  * the Jacobi round (calibration.cu) pairs each local row with the partner and rotation
+    (j, p-or-q) of the reference's round-robin schedule.
+"""
+
+import numpy as np
+import torch
+
+from oracle.calibration_oracle import round_robin_pairs
+from oracle.int2_oracle import unpack
+
+
+def prmt(a: int, b: int, sel: int) -> int:
+    """PTX prmt.b32 (default mode): byte i of the result is byte (nibble i & 7) of the
+    eight bytes b:a, or that byte's sign replicated when nibble bit 3 is set."""
+    pool = [(a >> (8 * k)) & 0xFF for k in range(4)] + [(b >> (8 * k)) & 0xFF for k in range(4)]
+    out = 0
+    for i in range(4):
+        nib = (sel >> (4 * i)) & 0xF
+        byte = pool[nib & 7]
+        if nib & 8:
+            byte = 0xFF if byte & 0x80 else 0x00
+        out |= byte << (8 * i)
+    return out
+
+
+def half_bits(x: float) -> int:
+    return int(np.array([x], dtype=np.float16).view(np.uint16)[0])
+
+
+def bf16(x):
+    return torch.tensor(x, dtype=torch.float32).bfloat16().float().numpy()
+
+
+def key_table(s: np.float16, z: np.float16):
+    """key_lut: the four levels bf16(c*s + z), scaled by 2^e into [2^14, 2^15), as fp16
+    byte planes (lo = low bytes, hi = high bytes); returns (lo, hi, scaled levels)."""
+    sf, zf = np.float32(s), np.float32(z)
+    v = bf16([zf, np.float32(sf + zf), np.float32(np.float32(2) * sf + zf), np.float32(np.float32(3) * sf + zf)])
+    ex = (np.array([max(abs(v[0]), abs(v[3]))], dtype=np.float32).view(np.uint32)[0] >> 23) & 0xFF
+    exc = max(int(ex), 16)
+    up = np.array([(268 - exc) << 23], dtype=np.uint32).view(np.float32)[0]
+    scaled = (v * up).astype(np.float32)
+    h = [half_bits(x) for x in scaled]
+    h01, h23 = h[0] | (h[1] << 16), h[2] | (h[3] << 16)
+    return prmt(h01, h23, 0x6420), prmt(h01, h23, 0x7531), scaled
+
+
+def test_key_selectors_fetch_the_bf16_levels_for_every_code_byte():
+    rng = np.random.default_rng(7)
+    cases = [(np.float16(0.5), np.float16(-0.75)), (np.float16(2.0 ** -14), np.float16(0.0)),
+             (np.float16(3000.0), np.float16(-60000.0))]
+    cases += [(np.float16(abs(rng.normal()) * 10 ** rng.uniform(-3, 2) + 2 ** -14), np.float16(rng.normal() * 30))
+              for _ in range(40)]
+    for s, z in cases:
+        lo, hi, levels = key_table(s, z)
+        # the scaled levels are exact in fp16
+        assert np.array_equal(levels.astype(np.float16).astype(np.float32), levels)
+        for word in range(256):
+            codes = [(word >> (2 * p)) & 3 for p in range(4)]
+            x = sum(c << (8 * k) for k, c in enumerate(codes))  # codes of one position, bytes 0..3
+            sel = (x * 0x11 + 0x40404040) & 0xFFFFFFFF
+            for half, pair in ((sel & 0xFFFF, codes[:2]), (sel >> 16, codes[2:])):
+                r = prmt(lo, hi, half)
+                got = np.array([r & 0xFFFF, r >> 16], dtype=np.uint16).view(np.float16).astype(np.float32)
+                assert np.array_equal(got, levels[pair]), (s, z, word)
+
+
+def test_bf16_counts_are_exact_small_integers():
+    one, zero = torch.tensor(1.0).bfloat16(), torch.tensor(0.0).bfloat16()
+    for lo_counts in np.ndindex(5, 5):
+        for hi_counts in np.ndindex(5, 5):
+            halves = []
+            for c0, c1 in (lo_counts, hi_counts):
+                a0 = torch.tensor(32.0).bfloat16()
+                a1 = torch.tensor(32.0).bfloat16()
+                for i in range(4):
+                    a0 = a0 + (one if i < c0 else zero)
+                    a1 = a1 + (one if i < c1 else zero)
+                halves.append(a0 + a1)
+            total = halves[0] + halves[1]
+            bits = int(total.view(torch.int16).item()) & 0xFFFF
+            assert bits & 0x7F == sum(lo_counts) + sum(hi_counts)
+
+
+def test_mtp_value_byte_lanes_partition_the_dims():
+    dims = [32 * gi + 16 * half + 4 * w + p for w in range(4) for gi in range(8) for half in range(2)
+            for p in range(4)]
+    assert sorted(dims) == list(range(256))
+    # warp w's operand: prmt(word of token a, same word of token b, vsel) >> vshift, then
+    # mask 0x00030003 << 2p: token a's code in bits 2p..2p+1, token b's 16 bits higher
+    rng = np.random.default_rng(11)
+    vecs = np.zeros((2, 68), dtype=np.uint8)
+    vecs[:, :64] = rng.integers(0, 256, size=(2, 64), dtype=np.uint8)
+    vecs[:, 64:66] = np.array([1.0], dtype=np.float16).view(np.uint8)  # scale 1, zero 0
+    codes = unpack(vecs).float().numpy().astype(int)
+    words = vecs[:, :64].copy().view("<u4")
+    for w in range(4):
+        vsel = 0x7632 if w >> 1 else 0x5410
+        vshift = 8 if w & 1 else 0
+        for gi in range(8):
+            for half in range(2):
+                x = prmt(int(words[0, 2 * gi + half]), int(words[1, 2 * gi + half]), vsel) >> vshift
+                for p in range(4):
+                    d = 32 * gi + 16 * half + 4 * w + p
+                    assert (x >> (2 * p)) & 3 == codes[0, d]
+                    assert (x >> (16 + 2 * p)) & 3 == codes[1, d]
+
+
+def mod_dm1(x, d=256):
+    x += (d - 1) if x < 0 else 0
+    return x - (d - 1) if x >= d - 1 else x
+
+
+def test_jacobi_row_partners_follow_the_round_robin_schedule():
+    d = 256
+    for r in range(d - 1):
+        p, q = (t.tolist() for t in round_robin_pairs(d, r))
+        for x in range(d):
+            if x == d - 1:
+                y, j, isp = r, 0, 1
+            elif x == r:
+                y, j, isp = d - 1, 0, 0
+            else:
+                y = mod_dm1(mod_dm1(2 * r - x))
+                jp = mod_dm1(x - r)
+                j, isp = (jp, 1) if 1 <= jp < d // 2 else (mod_dm1(r - x), 0)
+            assert (p[j], q[j]) == ((x, y) if isp else (y, x)), (r, x)
