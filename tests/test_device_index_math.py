@@ -10,7 +10,10 @@ arithmetic those kernels rely on, over every case rather than a sample:
   * the MTP kernel's value byte lanes (history_mtp.cu) split the 256 dims among the four
     warps of a head and extract the codes the reference's unpack assigns to those dims;
   * the Jacobi round (calibration.cu) pairs each local row with the partner and rotation
-    (j, p-or-q) of the reference's round-robin schedule.
+    (j, p-or-q) of the reference's round-robin schedule;
+  * the rotation epilogue's row -> (token, head) split by multiply-high (rotate.cuh);
+  * the window store (attention.cu `window_store_kernel`) visits exactly the reference's
+    per-slot latest writers, each slot once.
 """
 
 import numpy as np
@@ -136,3 +139,53 @@ def test_jacobi_row_partners_follow_the_round_robin_schedule():
                 jp = mod_dm1(x - r)
                 j, isp = (jp, 1) if 1 <= jp < d // 2 else (mod_dm1(r - x), 0)
             assert (p[j], q[j]) == ((x, y) if isp else (y, x)), (r, x)
+
+
+def test_row_to_token_division_by_multiply_high():
+    # rotate.cuh: floor(t / h) = umulhi(t, floor((2^32 - 1) / h) + 1) for t < 2^16 (t is
+    # a tile's first head plus a row offset); every head count a token can have
+    t = np.arange(1 << 16, dtype=np.uint64)
+    for h in range(2, 257):
+        hm = np.uint64(0xFFFFFFFF // h + 1)
+        tq = (t * hm) >> np.uint64(32)
+        assert np.array_equal(tq, t // np.uint64(h)), h
+        assert np.array_equal(t - tq * np.uint64(h), t % np.uint64(h)), h
+
+
+def window_positions_visited(seq, qlen, sink, ring):
+    """window_store_kernel's loop: sink [lo, min(seq, S)), ring [max(lo, S, seq - C), seq)."""
+    if qlen <= 0:
+        return []
+    lo = max(seq - qlen, 0)
+    n_sink = max(0, min(seq, sink) - lo)
+    ring_lo = max(lo, sink, seq - ring)
+    n_ring = max(0, seq - ring_lo)
+    out = []
+    for k in range(n_sink + n_ring):
+        pos = lo + k if k < n_sink else ring_lo + (k - n_sink)
+        out.append((pos if pos < sink else sink + pos % ring, pos))
+    return out
+
+
+def window_positions_reference(seq, qlen, sink, ring):
+    """Per-slot latest-writer rule of int2_oracle.store_windows."""
+    prefix = seq - qlen
+    out = []
+    for idx in range(sink + ring):
+        pos = idx if idx < sink else seq - 1 - ((seq - 1 - (idx - sink)) % ring)
+        if pos >= prefix and pos < seq and qlen > 0 and (idx < sink or pos >= sink):
+            out.append((idx, pos))
+    return out
+
+
+def test_window_store_visits_each_slots_latest_writer_once():
+    for sink in (0, 1, 4, 16):
+        for ring in (1, 3, 8, 32):
+            for seq in range(0, 90):
+                for qlen in sorted({0, 1, 2, 3, 5, 8, 17, 40, seq}):
+                    if qlen > seq:
+                        continue
+                    got = window_positions_visited(seq, qlen, sink, ring)
+                    assert len({idx for idx, _ in got}) == len(got)  # no slot written twice
+                    assert sorted(got) == window_positions_reference(seq, qlen, sink, ring), (
+                        sink, ring, seq, qlen)
