@@ -66,31 +66,6 @@ OSCAR_DEVINL TaskInfo load_task(int task, const int32_t *tasks, const int32_t *t
   return ti;
 }
 
-// Per-token coefficients of q.k with k = bf16(c*s + z) (the reference rounds the
-// dequantised key to bf16), as the tcgen05 kernel uses them:
-//   q.k = v0*sum(q) + (v1-v0)*sum(q c) + a*sum(q b1) + b*sum(q b0 b1)
-// with v_c = bf16(c*s + z), a = v2 - 2 v1 + v0, b = v3 - v2 - v1 + v0.  Since
-// sum(q c) = sum(q b0) + 2 sum(q b1), with the three MMA sums M = sum(q c),
-// A = sum(q b0), C = sum(q b0 b1) over the code, b0 and b0b1 planes:
-//   q.k = v0*sum(q) + (d1 + a/2) M - (a/2) A + b C.
-struct KeyCoef {
-  float v0, d1, a, b;
-};
-
-OSCAR_DEVINL KeyCoef key_coefficients(uint32_t sz) {
-  const float s = half_bits_to_float(sz & 0xffffu), z = half_bits_to_float(sz >> 16);
-  const float v0 = round_bf16(z);
-  const float v1 = round_bf16(__fadd_rn(s, z));
-  const float v2 = round_bf16(__fadd_rn(2.f * s, z));
-  const float v3 = round_bf16(__fadd_rn(3.f * s, z));
-  KeyCoef k;
-  k.v0 = v0;
-  k.d1 = v1 - v0;
-  k.a = (v2 - v1) - (v1 - v0);
-  k.b = (v3 - v2) - (v1 - v0);
-  return k;
-}
-
 // The four bf16 key levels v_c = bf16(c*s + z) of one token as an fp16 byte table for
 // PRMT: levels scaled by 2^e (max |v| in [2^14, 2^15)), which fp16 holds exactly (a
 // level smaller than 2^-31 max |v| may lose low bits).  lo = low bytes of the four
