@@ -12,8 +12,6 @@ uses them.
 
 from __future__ import annotations
 
-import math
-
 import torch
 
 from . import _lib
@@ -285,7 +283,3 @@ def decode_attention(qrot, query, key, value, history, window, meta, layout, sca
               scratch.lse.data_ptr(), output.data_ptr(), geo, float(scale), int(splits), window_programs,
               _stream(query))
     return output
-
-
-def default_scale(head_dim: int = 256) -> float:
-    return 1.0 / math.sqrt(head_dim)

@@ -46,10 +46,6 @@ def outlier_bf16(gen: torch.Generator, *shape, channels: int = 8, factor: float 
     return x.bfloat16().to(device)
 
 
-def normal_bf16(gen: torch.Generator, *shape, device="cpu"):
-    return torch.randn(*shape, generator=gen).bfloat16().to(device)
-
-
 @dataclass
 class PagedPlan:
     """Page ownership and per-step metadata for a batch of requests (host tensors)."""
