@@ -7,7 +7,6 @@ eigensolver is ``torch.linalg.eigh`` + the oracle's ``U H P_br`` composition."""
 
 import os
 import socket
-from types import SimpleNamespace
 
 import pytest
 import torch

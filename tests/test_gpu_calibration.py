@@ -11,7 +11,6 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from oracle import calibration_oracle as co
 from oscar_new_b200.calibration_worker import CalibrationSession
 from tests.test_calibration_worker import activations, expected_stack
 
