@@ -4,6 +4,8 @@ import ctypes
 import re
 from pathlib import Path
 
+import pytest
+
 from oscar_new_b200 import _lib
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -50,3 +52,18 @@ def test_sst_weights_reject_keys_that_are_not_16_byte_rows():
         assert fn(ok_ptr, 1, 1, 260, 256, ok_ptr, ok_ptr, ok_ptr, None) == 1
         assert fn(ok_ptr, 1, 1, 256, 260, ok_ptr, ok_ptr, ok_ptr, None) == 1
         assert fn(ok_ptr, 0, 1, 260, 260, ok_ptr, ok_ptr, ok_ptr, None) == 0  # nothing to do
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_PATH", tmp_path / "liboscar_b200.so")
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(RuntimeError, match="not built"):
+        _lib.lib()
+
+
+@pytest.mark.parametrize("status,text", [(1, "invalid argument"), (2, "launch error"), (3, "unsupported"),
+                                         (4, "device wait timeout")])
+def test_nonzero_status_raises_with_its_name(status, text):
+    with pytest.raises(RuntimeError, match=f"^oscar_store_int2 failed: {text}$"):
+        _lib.check(status, "oscar_store_int2")
+    _lib.check(0, "oscar_store_int2")
