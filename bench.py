@@ -129,10 +129,19 @@ LAUNCHES_PER_STEP = 6  # tasks, rotate+store, history, raw, finalize, window sto
 
 class ClockSampler:
     """nvidia-smi samples (every 20 ms) of this GPU's SM clock and throttle reasons;
-    `mark()` brackets the timed region and `summary()` keeps the samples inside it."""
+    `mark()` brackets the timed region and `summary()` keeps the samples inside it.
+    Every GPU is sampled and the rows are matched to this device by PCI bus id, since
+    nvidia-smi's index need not equal the CUDA ordinal (CUDA_VISIBLE_DEVICES); the
+    ordinal is the fallback when no row matches."""
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, device):
+        device = torch.device(device)
+        self.index = device.index if device.index is not None else torch.cuda.current_device()
+        try:
+            prop = torch.cuda.get_device_properties(self.index)
+            self.bus = (prop.pci_domain_id, prop.pci_bus_id, prop.pci_device_id)
+        except (RuntimeError, AttributeError, AssertionError):
+            self.bus = None
         self.proc = None
         self.path = None
         self.window = None
@@ -140,12 +149,12 @@ class ClockSampler:
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
-        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("timestamp,index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "20"],
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -167,18 +176,24 @@ class ClockSampler:
         if not self.path or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        samples = []
+        by_bus, by_index = [], []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 10:
+            if len(parts) < 11:
                 continue
             try:
                 ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                samples.append((ts, float(parts[2]), float(parts[3]),
-                                {n for n, v in zip(names, parts[6:10]) if v.lower() == "active"}))
+                row = (ts, float(parts[3]), float(parts[4]),
+                       {n for n, v in zip(names, parts[7:11]) if v.lower() == "active"})
+                dom, bus, devfn = parts[2].split(":")
+                if self.bus is not None and (int(dom, 16), int(bus, 16), int(devfn.split(".")[0], 16)) == self.bus:
+                    by_bus.append(row)
+                if int(parts[1]) == self.index:
+                    by_index.append(row)
             except ValueError:
                 continue
         os.unlink(self.path)
+        samples = by_bus or by_index
         if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         inside = samples
@@ -242,7 +257,7 @@ def run_gpu(args):
     barrier()
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(device) as clocks:
         t0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):
@@ -593,7 +608,7 @@ def run_rotate_store(args):
         kernels.rotate_store(st["k"], st["v"], st["rk"], st["rv"], st["history"], st["slots"], st["counts"],
                              st["layout"])
 
-    with ClockSampler(0) as clocks:
+    with ClockSampler(device) as clocks:
         t0 = time.time()
         ms = _timed_each(step, args.steps, args.warmup, device, flush)
         clocks.mark(t0, time.time())
@@ -723,7 +738,7 @@ def run_mtp_verify(args):
         step()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clocks:
+    with ClockSampler(device) as clocks:
         t0 = time.time()
         e0.record(stream)
         for _ in range(args.steps):

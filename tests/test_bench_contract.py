@@ -1,9 +1,11 @@
-"""bench.py's reference arm on the CPU: the JSON line it prints and its rank rule.
+"""bench.py on the CPU: the reference arm's JSON line and rank rule, and how the clock
+samples taken during a timed region are matched to the measured device.
 
 The reference arm times the CPU oracle on host cores, so it runs without a GPU; the GPU
 arm's line is checked on the B200 by the driver itself.
 """
 
+import datetime
 import json
 import os
 import subprocess
@@ -46,3 +48,29 @@ def test_reference_arm_other_ranks_exit_without_work():
                   env_extra={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_clock_samples_follow_the_device_by_pci_bus_id(tmp_path):
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    rows = []
+    for k, t in enumerate(("05:00:00.100", "05:00:00.200", "05:00:00.300")):
+        # nvidia-smi index 0 is another GPU at 1000 MHz; index 1 is this device at 1965 MHz
+        rows.append(f"2026/12/02 {t}, 0, 00000000:18:00.0, 1000, 1965, 100.0, 0x0, Not Active, Not Active, "
+                    f"Not Active, Not Active")
+        rows.append(f"2026/12/02 {t}, 1, 00000000:2A:00.0, {1965 - k}, 1965, 700.0, 0x4, Not Active, Not Active, "
+                    f"Not Active, Active")
+    ts = [datetime.datetime(2026, 12, 2, 5, 0, 0, 100000 * i).timestamp() for i in (1, 2, 3)]
+
+    def sampler(bus, index):
+        s = bench.ClockSampler.__new__(bench.ClockSampler)
+        s.index, s.bus, s.proc, s.window = index, bus, None, (ts[0] - 0.01, ts[1] + 0.01)
+        s.path = str(tmp_path / f"clocks_{index}_{bus}.csv")
+        Path(s.path).write_text("\n".join(rows) + "\n")
+        return s
+
+    got = sampler((0, 0x2A, 0), 0).summary()  # CUDA ordinal 0 is nvidia-smi index 1
+    assert got["sm_mhz"] == 1964.5 and got["samples"] == 2 and got["reasons"] == ["sw_power_cap"]
+    got = sampler(None, 0).summary()  # no bus id: fall back to the ordinal
+    assert got["sm_mhz"] == 1000.0 and got["reasons"] == []
