@@ -1,4 +1,5 @@
-"""The C-ABI library loads on a CPU host and exports every symbol the header declares."""
+"""The C-ABI library loads on a CPU host, exports every symbol the header declares, and
+the structs the host passes by value have the header's layout."""
 
 import ctypes
 import re
@@ -67,3 +68,30 @@ def test_nonzero_status_raises_with_its_name(status, text):
     with pytest.raises(RuntimeError, match=f"^oscar_store_int2 failed: {text}$"):
         _lib.check(status, "oscar_store_int2")
     _lib.check(0, "oscar_store_int2")
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """sizeof / offsetof of oscar_geometry and oscar_clip as gcc lays them out from the
+    header, against the ctypes structures the host passes by value."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    fields = {"oscar_geometry": _lib.Geometry, "oscar_clip": _lib.Clip}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "oscar_b200.h"', "int main(void) {"]
+    for cname, cls in fields.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                              check=True).stdout.splitlines())
+    for cname, cls in fields.items():
+        assert int(got[f"{cname} size"]) == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert int(got[f"{cname} {fname}"]) == getattr(cls, fname).offset, (cname, fname)
