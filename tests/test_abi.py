@@ -95,3 +95,27 @@ def test_ctypes_structs_match_the_header_layout(tmp_path):
         assert int(got[f"{cname} size"]) == ctypes.sizeof(cls), cname
         for fname, _ in cls._fields_:
             assert int(got[f"{cname} {fname}"]) == getattr(cls, fname).offset, (cname, fname)
+
+
+def _ctype_of(param: str):
+    """ctypes class of one C parameter declaration of the header."""
+    p = " ".join(param.replace("const ", "").split())
+    if "*" in p:
+        return ctypes.c_void_p
+    kind = p.rsplit(" ", 1)[0] if " " in p else p
+    return {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
+            "oscar_geometry": _lib.Geometry, "oscar_clip": _lib.Clip, "void": None}[kind]
+
+
+def test_binding_argument_types_follow_the_header_prototypes():
+    text = (ROOT / "include" / "oscar_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    protos = re.findall(r"^(int|int64_t) (oscar_\w+)\((.*?)\);", text, flags=re.M | re.S)
+    assert protos
+    for ret, name, params in protos:
+        want = [t for t in (_ctype_of(x) for x in params.split(",")) if t is not None]
+        got = _lib._SIGNATURES[name]
+        assert len(got) == len(want), (name, len(got), len(want))
+        for i, (g, w) in enumerate(zip(got, want)):
+            assert g is w, (name, i, g, w)
+        assert _lib._RESTYPES.get(name, ctypes.c_int) is (ctypes.c_int64 if ret == "int64_t" else ctypes.c_int), name
