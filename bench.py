@@ -48,6 +48,13 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def decode_config():
+    """The decode workload both arms report (config 3)."""
+    return {"workload": "config3 single-query paged INT2 decode attention layer (store + attention + merge)",
+            "requests_per_gpu": B, "context": SEQ, "q_heads": H * G, "kv_heads": H, "head_dim": D,
+            "sink": SINK, "recent": RECENT, "kv_splits": SPLITS, "page_tokens": BP}
+
+
 def workload_sizes():
     hist_tokens = SEQ - 1 - SINK - RECENT  # prefix minus sink and recent
     hist_bytes = B * H * hist_tokens * HISTORY_BYTES_PER_TOKEN_HEAD
@@ -370,9 +377,7 @@ def run_gpu(args):
             "dtype": "int2-kv/bf16",
             "data": "synthetic (seeded N(0,1) bf16, K channels 0-7 x20, random-permutation pages)",
             "config": {
-                "workload": "config3 single-query paged INT2 decode attention layer (store + attention + merge)",
-                "requests_per_gpu": B, "context": SEQ, "q_heads": H * G, "kv_heads": H, "head_dim": D,
-                "sink": SINK, "recent": RECENT, "kv_splits": SPLITS, "page_tokens": BP,
+                **decode_config(),
                 "l2": "inputs larger than L2 (packed history 1.14 GB per GPU)",
                 "us_per_layer": step_ms * 1e3,
                 "hbm_gbs_algorithmic": sizes["algorithmic_bytes"] / (step_ms * 1e-3) / 1e9,
@@ -536,8 +541,11 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "int2-kv/fp32",
         "data": "synthetic (seeded, same generators as the GPU arm)",
-        "config": {"workload": "config3 decode attention, one request per step (bounded CPU sample)",
-                   "context": SEQ, "q_heads": H * G, "kv_heads": H, "head_dim": D},
+        "config": {**decode_config(),
+                   "sample": f"one of the {B} requests per step (bounded CPU sample): attention, merges and inverse "
+                             f"rotation through the CPU oracle; the INT2 and window stores of the current token (1 "
+                             f"of the request's {SEQ}) are not in it",
+                   "parallelism": f"{torch.get_num_threads()} host threads, rank 0 only"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": "1 config-3 request (32768 tokens x 4 KV heads) per step through the CPU oracle"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -35,7 +35,11 @@ def test_reference_arm_prints_one_contract_line():
     assert line["steps"] == 1 and line["warmup"] >= 3  # fewer than 3 warm-up steps are raised to 3
     assert line["higher_is_better"] is True and line["scaling"] == "weak" and line["n_gpus"] == 1
     assert line["value"] > 0 and line["ms_per_step"] > 0
-    assert "workload" in line["config"]
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for key, val in bench.decode_config().items():  # the GPU arm's workload, sampled
+        assert line["config"][key] == val, key
     cb = line["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == line["value"]
     assert cb["unit"] == line["unit"] and cb["sample"]
@@ -74,3 +78,4 @@ def test_clock_samples_follow_the_device_by_pci_bus_id(tmp_path):
     assert got["sm_mhz"] == 1964.5 and got["samples"] == 2 and got["reasons"] == ["sw_power_cap"]
     got = sampler(None, 0).summary()  # no bus id: fall back to the ordinal
     assert got["sm_mhz"] == 1000.0 and got["reasons"] == []
+
