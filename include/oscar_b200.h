@@ -35,6 +35,15 @@ enum {
   OSCAR_ERR_TIMEOUT = 4    /* a bounded device wait gave up (reported via status buffer) */
 };
 
+/* Device status word.  Entry points whose kernels wait on the device (mbarrier phases of
+ * asynchronous copies and tensor-core work) take `int32_t *status`: a device int32, or
+ * NULL.  Every such wait gives up after a fixed number of probes instead of hanging; the
+ * kernel then stores OSCAR_ERR_TIMEOUT into *status, stops consuming, lets its copies in
+ * flight land, frees its tensor memory and returns, leaving the context usable.  The
+ * library never clears the word: the caller zeroes it, and reads it after synchronising
+ * the stream (a nonzero value means the outputs of the calls since it was zeroed are not
+ * valid).  Launch-time errors are still the return value. */
+
 /* Cache geometry shared by the paged kernels (reference oscar_ascend/layout.py:8-95,
  * config.py:46-63).  page_bytes = physical_block_tokens * kv_heads * head_dim * 2. */
 typedef struct oscar_geometry {
@@ -102,7 +111,7 @@ int oscar_rotate_store(const void *key, int64_t ks0, int64_t ks1, const void *va
                        const int64_t *slots, const int32_t *counts, oscar_geometry geo,
                        oscar_clip kclip, oscar_clip vclip, const void *query, int64_t qs0,
                        int64_t qs1, int32_t hq, void *qrot_out, void *krot_out, void *vrot_out,
-                       void *stream);
+                       int32_t *status, void *stream);
 
 /* Compact (request, query-offset) task table + optional page-table column copy.
  * Replaces reference kernels.py:222-287 (prepare_tasks / _prepare_tasks_kernel).
@@ -125,7 +134,7 @@ int oscar_attention_partials(const void *query, int64_t qs0, int64_t qs1, const 
                              const int32_t *table, const int32_t *counts, const int32_t *tasks,
                              const int32_t *task_count, int32_t num_tasks, int64_t n,
                              float *partials, float *lse, oscar_geometry geo, float scale,
-                             int32_t splits, int32_t raw, void *stream);
+                             int32_t splits, int32_t raw, int32_t *status, void *stream);
 
 /* LSE merge of split partials -> bf16 out [n,Hq,256] + fp32 logsum [n,Hq]; every row
  * is written (rows >= counts[1] get 0 / -inf).  Reference kernels.py:485-511. */
@@ -169,7 +178,7 @@ int oscar_decode_attention(const void *qrot, const void *query, int64_t qs0, int
                            const int32_t *task_count, int32_t num_tasks, int64_t n,
                            const void *rv, float *scratch_partials, float *scratch_lse,
                            void *output, oscar_geometry geo, float scale, int32_t splits,
-                           int32_t window_programs, void *stream);
+                           int32_t window_programs, int32_t *status, void *stream);
 
 /* oscar_decode_attention without caller scratch, for callers that cannot allocate
  * device memory during decode (an engine whose memory plan already gave all free
@@ -178,8 +187,10 @@ int oscar_decode_attention(const void *qrot, const void *query, int64_t qs0, int
  * oscar_decode_attention_noalloc_max_rows() rows (n * Hq * (splits + 1) <= 32768, i.e.
  * 32 MiB of partials) held by every GPU that loads the library; larger calls return
  * OSCAR_ERR_INVALID.  The first call on a device looks up the array's address (make it
- * before any stream capture).  All calls on a device share the array, so calls whose GPU
- * work overlaps race; sequential calls need no clearing.  Nothing is allocated. */
+ * before any stream capture; a first call on a capturing stream returns
+ * OSCAR_ERR_INVALID).  The looked-up address belongs to the device's primary context.
+ * All calls on a device share the array, so calls whose GPU work overlaps race;
+ * sequential calls need no clearing.  Nothing is allocated. */
 int oscar_decode_attention_noalloc(const void *qrot, const void *query, int64_t qs0, int64_t qs1,
                                    const void *key, int64_t ks0, int64_t ks1, const void *value,
                                    int64_t vs0, int64_t vs1, const uint8_t *history, void *window,
@@ -188,7 +199,7 @@ int oscar_decode_attention_noalloc(const void *qrot, const void *query, int64_t 
                                    const int32_t *tasks, const int32_t *task_count,
                                    int32_t num_tasks, int64_t n, const void *rv, void *output,
                                    oscar_geometry geo, float scale, int32_t splits,
-                                   int32_t window_programs, void *stream);
+                                   int32_t window_programs, int32_t *status, void *stream);
 
 /* Row capacity of the built-in scratch of oscar_decode_attention_noalloc. */
 int64_t oscar_decode_attention_noalloc_max_rows(void);

@@ -54,21 +54,21 @@ _SIGNATURES = {
     "oscar_selftest_bounded_wait": [P, P],
     "oscar_rotate": [P, I64, I32, I64, I64, I64, P, I64, I64, P, P],
     "oscar_store_int2": [P, P, I64, P, P, P, Geometry, Clip, Clip, P],
-    "oscar_rotate_store": [P, I64, I64, P, I64, I64, I64, P, P, P, P, P, Geometry, Clip, Clip, P, I64, I64, I32, P, P, P, P],
+    "oscar_rotate_store": [P, I64, I64, P, I64, I64, I64, P, P, P, P, P, Geometry, Clip, Clip, P, I64, I64, I32, P, P, P, P, P],
     "oscar_prepare_tasks": [P, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P],
-    "oscar_attention_partials": [P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P],
+    "oscar_attention_partials": [P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P, P],
     "oscar_merge_splits": [P, P, I64, I32, I32, P, P, P, P],
     "oscar_merge_paths": [P, P, P, I64, P, I64, I64, I32, P, P, P],
     "oscar_store_windows": [P, I64, I64, P, I64, I64, P, P, P, P, P, I32, Geometry, P],
     "oscar_unpack": [P, P, I64, Geometry, P, P, P],
-    "oscar_decode_attention": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, P, P, Geometry, F32, I32, I32, P],
+    "oscar_decode_attention": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, P, P, Geometry, F32, I32, I32, P, P],
     "oscar_accumulate_gram": [P, I64, I32, I64, I64, P, P, P],
     "oscar_sst_weights": [P, I64, I32, I64, I64, P, P, P, P],
     "oscar_accumulate_gram_grouped": [P, I64, I32, I64, I64, I32, P, P, P],
     "oscar_sst_weights_per_head": [P, I64, I32, I64, I64, P, P, P, P],
     "oscar_normalize": [P, I64, P, F32, P, P],
     "oscar_jacobi_rotations": [P, I32, I32, F32, P, P, P, P],
-    "oscar_decode_attention_noalloc": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P],
+    "oscar_decode_attention_noalloc": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P, P],
     "oscar_decode_attention_noalloc_max_rows": [],
 }
 _RESTYPES = {"oscar_decode_attention_noalloc_max_rows": C.c_int64}

@@ -181,6 +181,9 @@ class OscarAttentionImpl(AttentionImpl):
                                                    value[a:b].transpose(0, 1).unsqueeze(0), is_causal=True,
                                                    enable_gqa=True, scale=self.scale)
                 out[a:b].copy_(o[0].transpose(0, 1))
+        # rows past the step's last request are padding (graph-sized batches): zero, as
+        # the reference does after its fused prefill attention
+        out[starts[meta.num_reqs]:].zero_()
         kernels.store_windows(key, value, self.window, meta, meta.layout)
         return output
 

@@ -97,11 +97,13 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + STAGES;
   uint8_t *stages = smem + 128;
+  __shared__ int32_t s_abort;  // any warp's wait gave up: the CTA's partials are not valid
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], P.consumers);
     }
+    s_abort = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -157,7 +159,10 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
     const int s = c % STAGES;
     if (!mbar_wait_bounded(&full[s], (c / STAGES) & 1)) {
       ok = false;
-      if (lane == 0 && P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
+      if (lane == 0) {
+        atomicExch(&s_abort, 1);
+        if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
+      }
       break;
     }
     const uint8_t *stage = stages + s * P.stage_bytes;
@@ -326,6 +331,7 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
       if (warp == c % P.consumers && lane == 0 && cn < nchunks) {
         if (cn >= STAGES && !mbar_wait_bounded(&empty[cn % STAGES], ((cn / STAGES) - 1) & 1)) {
           good = 0;
+          atomicExch(&s_abort, 1);
           if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
         } else {
           issue_one(cn);
@@ -372,6 +378,7 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
   aux[(warp * 4 + 3) * 32 + lane] = zp_run[1];
   asm volatile("bar.sync 1, %0;" ::"r"(P.consumers * 32));
   if (sub > 0) return;
+  const bool aborted = *reinterpret_cast<volatile int32_t *>(&s_abort) != 0;
   float mtot[2] = {m_run[0], m_run[1]};
   for (int w2 = warp + P.units; w2 < P.consumers; w2 += P.units) {
     const float *rec = xch + (size_t)(w2 - P.units) * kSlot;
@@ -408,10 +415,11 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
     const int tok = ti.qstart + ti.qoff + row / g.group;
     const int qh = head * g.group + row % g.group;
     const int64_t orow = ((int64_t)tok * g.kv_heads * g.group + qh) * P.split_slots + split;
-    const bool any = L[r] > 0.f;
+    // an aborted CTA marks its rows empty (-inf) so no merge reads a partial sum
+    const bool any = L[r] > 0.f && !aborted;
     // lse (natural log): m is in log2 units
     if (gi == 0) P.lse[orow] = any ? (mtot[r] * 0.69314718055994531f + logf(L[r])) : -INFINITY;
-    if (!any && P.balanced) continue;  // the merge skips -inf splits without reading them
+    if (!any && (P.balanced || aborted)) continue;  // the merge skips -inf splits without reading them
     const float inv = any ? 1.0f / L[r] : 0.f;
     const float zterm = any ? Z[r] * inv : 0.f;
     float *dst = P.partials + orow * kDim + 32 * gi;
@@ -1151,7 +1159,7 @@ extern "C" int oscar_attention_partials(const void *query, int64_t qs0, int64_t 
                                         const int32_t *seq_lens, const int32_t *table, const int32_t *counts,
                                         const int32_t *tasks, const int32_t *task_count, int32_t num_tasks,
                                         int64_t n, float *partials, float *lse, oscar_geometry geo, float scale,
-                                        int32_t splits, int32_t raw, void *stream) {
+                                        int32_t splits, int32_t raw, int32_t *status, void *stream) {
   if (!geo_ok(geo) || splits <= 0 || num_tasks < 0 || n < 0) return OSCAR_ERR_INVALID;
   if (n == 0 || num_tasks == 0) return OSCAR_OK;
   if (!query || !qstarts || !seq_lens || !table || !counts || !tasks || !task_count || !partials || !lse)
@@ -1187,6 +1195,7 @@ extern "C" int oscar_attention_partials(const void *query, int64_t qs0, int64_t 
   P.partials = partials, P.lse = lse, P.split_slots = splits, P.splits = splits;
   P.geo = geo;
   P.scale_log2 = scale * kLog2e;
+  P.status = status;
   return history_launch(P, num_tasks, (cudaStream_t)stream);
 }
 
@@ -1240,7 +1249,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
                                       const int32_t *tasks, const int32_t *task_count, int32_t num_tasks, int64_t n,
                                       const void *rv, float *scratch_partials, float *scratch_lse, void *output,
                                       oscar_geometry geo, float scale, int32_t splits, int32_t window_programs,
-                                      void *stream) {
+                                      int32_t *status, void *stream) {
   if (!geo_ok(geo) || splits <= 0 || splits > 64 || num_tasks < 0 || n < 0 || window_programs < 0)
     return OSCAR_ERR_INVALID;  // the fused merge holds at most 64 split LSEs per row in one warp
   if (n == 0) return OSCAR_OK;
@@ -1267,6 +1276,7 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
     H.scale_log2 = scale * kLog2e;
     H.balanced = 1;
     H.target_ctas = 8 * sm_count();
+    H.status = status;
     // history on the caller's stream at the greatest priority, the raw path and then the
     // window store beside it on the side stream (joined before the merge); without a side
     // stream, one after the other

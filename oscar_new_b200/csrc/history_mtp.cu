@@ -403,7 +403,19 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
       }
     }
   head_bar(hl);
-  if (!ok) return;
+  if (!ok) {
+    // aborted: mark the rows empty (-inf) so the merge never reads a partial sum
+    if (w == 0 && gi == 0)
+      for (int n = 0; n < NT; ++n)
+        for (int r = 0; r < 2; ++r) {
+          const int row = 8 * n + 2 * t + r;
+          if (row >= rows_valid) continue;
+          const int tok = ti.qstart + ti.qoff + row / g.group;
+          const int qh = head * g.group + row % g.group;
+          P.lse[((int64_t)tok * g.kv_heads * g.group + qh) * P.split_slots + split] = -INFINITY;
+        }
+    return;
+  }
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll

@@ -459,8 +459,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) history_tc_kernel(const __grid_
   }
   if (warp < 4) {
     named_sync(2, kTcThreads);  // pairs with the value warps' barrier 2
-    if (tid < R && !aborted(S)) {
-      const float L = S.lsum[tid];
+    if (tid < R) {  // an aborted CTA marks its rows empty so the merge skips them
+      const float L = aborted(S) ? 0.f : S.lsum[tid];
       P.lse[out_row(tid)] = L > 0.f ? (S.mfin[tid] * 0.69314718055994531f + logf(L)) : -INFINITY;
     }
   }

@@ -33,6 +33,7 @@ struct RotateParams {
   const int32_t *counts;
   oscar_geometry geo;
   oscar_clip clip[2];
+  int32_t *status;  // nullable device word: OSCAR_ERR_TIMEOUT when a bounded wait gave up
 };
 
 // Byte offset of a slot's head-0 vector pair in the history stripes, -1 for slot < 0.

@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 2) rotate_tc_kernel(const __grid_con
   tc_fence_after();
   __syncthreads();
   const bool ok = landed && *abort_flag == 0;
+  if (!ok && tid == 0 && P.rp.status) atomicExch(P.rp.status, OSCAR_ERR_TIMEOUT);
   __nv_bfloat16 *stage_rows = reinterpret_cast<__nv_bfloat16 *>(smem);  // 64 KiB of the 96
   if (ok && warp < 8) {
     const int q = warp & 3, half = warp >> 2;

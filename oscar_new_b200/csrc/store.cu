@@ -219,7 +219,7 @@ extern "C" int oscar_rotate_store(const void *key, int64_t ks0, int64_t ks1, con
                                   const int64_t *slots, const int32_t *counts, oscar_geometry geo,
                                   oscar_clip kclip, oscar_clip vclip, const void *query, int64_t qs0,
                                   int64_t qs1, int32_t hq, void *qrot_out, void *krot_out, void *vrot_out,
-                                  void *stream) {
+                                  int32_t *status, void *stream) {
   if (n < 0 || !geometry_ok(geo) || !clip_ok(kclip) || !clip_ok(vclip)) return OSCAR_ERR_INVALID;
   if (n == 0) return OSCAR_OK;
   if (!history || !slots || !counts) return OSCAR_ERR_INVALID;
@@ -234,6 +234,7 @@ extern "C" int oscar_rotate_store(const void *key, int64_t ks0, int64_t ks1, con
   p.geo = geo;
   p.clip[0] = kclip;
   p.clip[1] = vclip;
+  p.status = status;
   p.job[0] = RotateJob{reinterpret_cast<const __nv_bfloat16 *>(key), ks0, ks1, n, geo.kv_heads,
                        BMatrix{reinterpret_cast<const __nv_bfloat16 *>(rk), 256, 1},
                        reinterpret_cast<__nv_bfloat16 *>(krot_out), 0, tiles};

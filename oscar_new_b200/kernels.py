@@ -12,12 +12,54 @@ uses them.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
 from .config import attention_programs, quantile_weight_f32
 
 LOG2E = 1.4426950408889634
+
+# Device status words (one int32 per device).  Kernels with bounded device waits store
+# 4 (device wait timeout) into their device's word when a wait gives up; the library
+# never clears it.  With OSCAR_CHECK_STATUS=1 every such call synchronises and raises
+# on a nonzero word (debug mode); otherwise `read_status` reports it on demand.
+_STATUS_WORDS: dict = {}
+_CHECK_STATUS = os.environ.get("OSCAR_CHECK_STATUS", "0") not in ("", "0")
+
+
+def status_word(device) -> torch.Tensor:
+    """The int32[1] device status word that this module passes to ``device``'s launches."""
+    device = torch.device(device)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    word = _STATUS_WORDS.get(index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=f"cuda:{index}")
+        _STATUS_WORDS[index] = word
+    return word
+
+
+def read_status(device=None, clear: bool = True) -> int:
+    """Synchronise ``device`` and return its status word (0 = no device wait gave up)."""
+    word = status_word(device if device is not None else torch.device("cuda"))
+    torch.cuda.synchronize(word.device)
+    value = int(word.item())
+    if clear and value:
+        word.zero_()
+    return value
+
+
+def _status(t: torch.Tensor):
+    return status_word(t.device).data_ptr()
+
+
+def _checked(name: str, t: torch.Tensor):
+    """Debug mode: a launch whose device wait gave up raises instead of leaving stale outputs."""
+    if _CHECK_STATUS:
+        value = read_status(t.device)
+        if value:
+            raise RuntimeError(f"{name} failed on the device: {_lib.STATUS.get(value, value)}")
 
 
 def _stream(t: torch.Tensor):
@@ -137,7 +179,8 @@ def rotate_store(key, value, rk, rv, history, slots, counts, layout, query=None,
     _lib.call("oscar_rotate_store", key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(),
               value.stride(0), value.stride(1), n, rk.data_ptr(), rv.data_ptr(), history.data_ptr(),
               slots.data_ptr(), counts.data_ptr(), geo, clip_params(cfg, "k"), clip_params(cfg, "v"),
-              *qargs, _ptr(kout), _ptr(vout), _stream(key))
+              *qargs, _ptr(kout), _ptr(vout), _status(key), _stream(key))
+    _checked("oscar_rotate_store", key)
     if debug_rotated:
         return qrot, kout, vout
     return qrot
@@ -186,7 +229,8 @@ def attention_partials(query, key, value, history, window, meta, layout, scale, 
               history.data_ptr(), window.data_ptr(), meta.query_start_loc.data_ptr(), meta.seq_lens.data_ptr(),
               meta.block_tables.data_ptr(), meta.counts.data_ptr(), meta.tasks.data_ptr(),
               meta.task_count.data_ptr(), min(programs, meta.tasks.shape[0]), n, partials.data_ptr(),
-              lse.data_ptr(), geo, float(scale), int(splits), int(bool(raw)), _stream(query))
+              lse.data_ptr(), geo, float(scale), int(splits), int(bool(raw)), _status(query), _stream(query))
+    _checked("oscar_attention_partials", query)
     return partials, lse
 
 
@@ -281,5 +325,6 @@ def decode_attention(qrot, query, key, value, history, window, meta, layout, sca
               meta.block_tables.data_ptr(), meta.counts.data_ptr(), meta.tasks.data_ptr(),
               meta.task_count.data_ptr(), programs, n, rv.data_ptr(), scratch.partials.data_ptr(),
               scratch.lse.data_ptr(), output.data_ptr(), geo, float(scale), int(splits), window_programs,
-              _stream(query))
+              _status(query), _stream(query))
+    _checked("oscar_decode_attention", query)
     return output

@@ -258,7 +258,7 @@ def build_paged_case(cfg_mod, oracle, lengths, prefixes, hq, h, sink, recent, mt
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout (read-only)")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
