@@ -18,7 +18,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "liboscar_b200.so"
-SOURCES = ["store.cu", "rotate_tc.cu", "attention.cu", "history_tc.cu", "history_mtp.cu", "calibration.cu", "noalloc.cu"]
+SOURCES = ["store.cu", "rotate_tc.cu", "attention.cu", "history_f8.cu", "history_mtp.cu", "calibration.cu",
+           "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

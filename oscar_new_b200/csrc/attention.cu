@@ -1025,13 +1025,6 @@ static int sm_count() {
   return cache[dev];
 }
 
-// Opt-in switch for the tcgen05 history kernel, read at every launch (a getenv is far
-// below a launch's cost) so that one process can compare both paths.
-static bool history_tc_enabled() {
-  const char *v = getenv("OSCAR_HISTORY_TC");
-  return v != nullptr && v[0] == '1';
-}
-
 // The shared-operand MTP kernel serves 9..24 rows per KV head (at most 4 KV heads) by
 // default; OSCAR_HISTORY_MTP=0 (read at every launch) sends those launches to
 // history_attention_kernel, for comparisons.
@@ -1040,9 +1033,16 @@ static bool history_mtp_enabled() {
   return v == nullptr || v[0] != '0';
 }
 
+// The 8-bit tcgen05 kernel serves every geometry it covers by default; OSCAR_HISTORY_F8=0
+// (read at every launch) sends those launches to the kernels below, for comparisons.
+static bool history_f8_enabled() {
+  const char *v = getenv("OSCAR_HISTORY_F8");
+  return v == nullptr || v[0] != '0';
+}
+
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {
-  if (history_tc_enabled()) {
-    const int rc = history_tc_launch(P, num_tasks, stream);
+  if (history_f8_enabled()) {
+    const int rc = history_f8_launch(P, num_tasks, sm_count(), stream, priority);
     if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
   }
   if (history_mtp_enabled()) {

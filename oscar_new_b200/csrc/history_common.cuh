@@ -1,8 +1,8 @@
-// Definitions shared by the two INT2 history attention kernels (attention.cu:
-// mma.sync with register-built operands; history_tc.cu: tcgen05 with the key
-// operands in tensor memory): launch parameters, task decoding (reference
-// oscar_ascend/kernels.py:290-330), the per-token coefficients of the bf16-rounded key
-// (tcgen05 kernel) and the per-token byte tables of its four levels (mma.sync kernel).
+// Definitions shared by the INT2 history attention kernels (attention.cu and
+// history_mtp.cu: mma.sync with register-built operands; history_f8.cu: tcgen05 with
+// 8-bit operands): launch parameters, task decoding (reference
+// oscar_ascend/kernels.py:290-330) and the per-token byte tables of the four bf16 key
+// levels (mma.sync kernels).
 #pragma once
 
 #include "common.cuh"
@@ -144,9 +144,9 @@ OSCAR_DEVINL void load_query_frags(QueryFrags &Q, const __nv_bfloat16 *qrow, boo
   Q.qm[1] = __shfl_sync(0xffffffffu, down, 8 * t + 4);
 }
 
-// tcgen05 history kernel (history_tc.cu); OSCAR_ERR_UNSUPPORTED for geometries it does
-// not cover (more than 32 query rows per KV head, other slot sizes).
-int history_tc_launch(const HistParams &P, int32_t num_tasks, cudaStream_t stream);
+// 8-bit tcgen05 history kernel (history_f8.cu): up to 8 query rows per KV head (decode),
+// persistent CTAs (at most `sm_count`); OSCAR_ERR_UNSUPPORTED for other geometries.
+int history_f8_launch(const HistParams &P, int32_t num_tasks, int sm_count, cudaStream_t stream, int priority);
 
 // History kernel for 9..24 query rows per KV head (MTP verify; history_mtp.cu): four
 // warps per KV head build every key and value operand once for all the head's rows.

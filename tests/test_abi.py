@@ -103,7 +103,7 @@ def _ctype_of(param: str):
     if "*" in p:
         return ctypes.c_void_p
     kind = p.rsplit(" ", 1)[0] if " " in p else p
-    return {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
+    return {"int32_t": ctypes.c_int32, "uint32_t": ctypes.c_uint32, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
             "oscar_geometry": _lib.Geometry, "oscar_clip": _lib.Clip, "void": None}[kind]
 
 

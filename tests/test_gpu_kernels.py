@@ -412,28 +412,6 @@ def test_decode_step_matches_hybrid_reference(cuda_lib, name, seq, qlen, hq, h, 
 @pytest.mark.parametrize(
     "name,seq,qlen,hq,h,cfg,splits",
     [
-        ("gqa24x4", [700, 1500, 3000], [1, 1, 1], 24, 4, make_config(4, 128, 0), 16),
-        ("mtp_verify", [900, 2049, 1400], [4, 4, 3], 24, 4, make_config(4, 128, 3), 8),
-    ],
-)
-def test_decode_step_tcgen05_history_opt_in(cuda_lib, monkeypatch, name, seq, qlen, hq, h, cfg, splits):
-    """The opt-in tcgen05 history kernel (OSCAR_HISTORY_TC=1: key operands in tensor
-    memory) against the same dense hybrid reference; its execution is asserted by name."""
-    monkeypatch.setenv("OSCAR_HISTORY_TC", "1")
-    sc = Scenario(seq, qlen, hq=hq, h=h, cfg=cfg, seed=len(name))
-    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
-        out = sc.run_step(splits).float().cpu()
-        torch.cuda.synchronize()
-    names = {e.name for e in prof.events()}
-    assert any("history_tc_kernel" in nm for nm in names), names
-    expect, _ = sc.expected()
-    assert rel_err(out, expect) < 1e-2, rel_err(out, expect)
-    torch.testing.assert_close(out, expect, atol=0.035, rtol=0.04)
-
-
-@pytest.mark.parametrize(
-    "name,seq,qlen,hq,h,cfg,splits",
-    [
         ("mtp_verify", [900, 2049, 1400], [4, 4, 3], 24, 4, make_config(4, 128, 3), 8),
         ("skewed_balanced", [140, 9000, 333, 2, 1500], [4, 4, 1, 2, 4], 24, 4, make_config(4, 128, 3), 64),
         ("group4_16rows", [1300, 2600], [4, 4], 16, 4, make_config(4, 128, 3), 8),
