@@ -9,6 +9,7 @@ profiler.  Tolerances as elsewhere: output atol .035 / rtol .04 and rel 1e-2 in 
 import pytest
 import torch
 
+from oracle import int2_oracle as oo
 from oscar_new_b200 import _lib, kernels
 from oscar_new_b200.config import task_capacity
 from oscar_new_b200.layout import CacheLayout
@@ -32,9 +33,22 @@ def kernel_names(fn):
     return out, {e.name for e in prof.events()}
 
 
-def merged_lse(scratch, n):
-    """Logsumexp over the split slots (history splits + the raw slot) of a decode step."""
-    return torch.logsumexp(scratch.lse[:n].float(), dim=-1).cpu()
+def history_lse(scratch, n, splits):
+    """Logsumexp over the history split slots of a decode step's scratch (the raw path's
+    slot, index `splits`, left out)."""
+    return torch.logsumexp(scratch.lse[:n, :, :splits].float(), dim=-1).cpu()
+
+
+def oracle_history_lse(sc, qrot, k, v):
+    """History-path LSE of the kernel-faithful CPU oracle on the same bf16 rotated query
+    (the dense hybrid reference rotates the query in fp32, which moves logits by about
+    2^-9 relative and is not a 1e-3 LSE reference)."""
+    meta_cpu = type("M", (), {})()
+    for nm in ("query_start_loc", "seq_lens", "block_tables", "counts"):
+        setattr(meta_cpu, nm, getattr(sc.meta, nm).cpu())
+    _, lse = oo.attention_partials(qrot.cpu(), k.cpu(), v.cpu(), sc.history.cpu(), sc.window.cpu(), meta_cpu,
+                                   sc.layout, 1 / 16, 1, False)
+    return lse[:, :, 0]
 
 
 @pytest.mark.parametrize("index", [0, 2])
@@ -89,49 +103,54 @@ def test_f8_decode_step_matches_hybrid_reference(cuda_lib, name, seq, qlen, hq, 
     sc = Scenario(seq, qlen, hq=hq, h=h, cfg=cfg, seed=len(name) + 40)
     n = sum(qlen)
     scratch = kernels.DecodeScratch(n, hq, splits, DEV)
+    q, k, v = sc.current()
+    sc.prepare_tasks()
+    qrot = kernels.rotate_store(k, v, sc.rk.to(DEV), sc.rv.to(DEV), sc.history, sc.meta.slot_mapping,
+                                sc.meta.counts, sc.layout, query=q)
 
     def step():
-        q, k, v = sc.current()
-        sc.prepare_tasks()
-        qrot = kernels.rotate_store(k, v, sc.rk.to(DEV), sc.rv.to(DEV), sc.history, sc.meta.slot_mapping,
-                                    sc.meta.counts, sc.layout, query=q)
         out = torch.empty((n, hq * 256), dtype=torch.bfloat16, device=DEV)
         kernels.decode_attention(qrot, q, k, v, sc.history, sc.window, sc.meta, sc.layout, 1 / 16, splits,
-                                 sc.rv.to(DEV), out, scratch)
+                                 sc.rv.to(DEV), out, scratch, store_window=False)
         return out.view(n, hq, 256)
 
     out, names = kernel_names(step)
     assert any(F8 in nm for nm in names), names
-    expect, lse = sc.expected()
+    expect, _ = sc.expected()
     assert rel_err(out.cpu(), expect) < 1e-2, rel_err(out.cpu(), expect)
     torch.testing.assert_close(out.float().cpu(), expect, atol=0.035, rtol=0.04)
-    torch.testing.assert_close(merged_lse(scratch, n), lse, atol=1e-3, rtol=0)
+    got, want = history_lse(scratch, n, splits), oracle_history_lse(sc, qrot, k, v)
+    assert torch.equal(torch.isinf(got), torch.isinf(want))
+    fin = torch.isfinite(want)
+    torch.testing.assert_close(got[fin], want[fin], atol=1e-3, rtol=0)
 
 
 def test_f8_config3_full_context(cuda_lib):
     """BASELINE config 3 at full per-request size: 32768-token contexts (4 sink, 128
-    recent, 32635 INT2 history tokens each), 24 query / 4 KV heads, 16 splits; output and
-    merged LSE against the oracle's dense hybrid reference."""
+    recent, 32635 INT2 history tokens each), 24 query / 4 KV heads, 16 splits; output
+    against the oracle's dense hybrid reference, history LSE against the oracle's
+    paged history attention."""
     seq = [32768] * 4
     sc = Scenario(seq, [1] * 4, hq=24, h=4, cfg=make_config(4, 128, 0), seed=33)
     scratch = kernels.DecodeScratch(4, 24, 16, DEV)
     q, k, v = sc.current()
     sc.prepare_tasks()
 
+    qrot = kernels.rotate_store(k, v, sc.rk.to(DEV), sc.rv.to(DEV), sc.history, sc.meta.slot_mapping,
+                                sc.meta.counts, sc.layout, query=q)
+
     def step():
-        qrot = kernels.rotate_store(k, v, sc.rk.to(DEV), sc.rv.to(DEV), sc.history, sc.meta.slot_mapping,
-                                    sc.meta.counts, sc.layout, query=q)
         out = torch.empty((4, 24 * 256), dtype=torch.bfloat16, device=DEV)
         kernels.decode_attention(qrot, q, k, v, sc.history, sc.window, sc.meta, sc.layout, 1 / 16, 16,
-                                 sc.rv.to(DEV), out, scratch)
+                                 sc.rv.to(DEV), out, scratch, store_window=False)
         return out.view(4, 24, 256)
 
     out, names = kernel_names(step)
     assert any(F8 in nm for nm in names), names
-    expect, lse = sc.expected()
+    expect, _ = sc.expected()
     assert rel_err(out.cpu(), expect) < 1e-2, rel_err(out.cpu(), expect)
     torch.testing.assert_close(out.float().cpu(), expect, atol=0.035, rtol=0.04)
-    torch.testing.assert_close(merged_lse(scratch, 4), lse, atol=1e-3, rtol=0)
+    torch.testing.assert_close(history_lse(scratch, 4, 16), oracle_history_lse(sc, qrot, k, v), atol=1e-3, rtol=0)
 
 
 def test_f8_wait_timeout_reports_status_and_context_recovers(cuda_lib):
