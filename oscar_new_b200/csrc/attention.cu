@@ -1033,11 +1033,13 @@ static bool history_mtp_enabled() {
   return v == nullptr || v[0] != '0';
 }
 
-// The 8-bit tcgen05 kernel serves every geometry it covers by default; OSCAR_HISTORY_F8=0
-// (read at every launch) sends those launches to the kernels below, for comparisons.
+// The 8-bit tcgen05 kernel (history_f8.cu) is opt-in: OSCAR_HISTORY_F8=1, read at every
+// launch.  It is parity-green but slower than history_attention_kernel on config 3
+// (1208 against 454 us per launch on B200): its warp roles run one warp per
+// sub-partition, each a latency-bound chain over thin (N = 16) tensor-core tiles.
 static bool history_f8_enabled() {
   const char *v = getenv("OSCAR_HISTORY_F8");
-  return v == nullptr || v[0] != '0';
+  return v != nullptr && v[0] == '1';
 }
 
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {

@@ -153,6 +153,20 @@ OSCAR_DEVINL bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may stay suspended for up to `hint_ns` nanoseconds
+// while the phase is incomplete (it resumes as soon as the phase completes): a waiting
+// warp sleeps instead of spinning and leaves its issue slots to the working warps.
+OSCAR_DEVINL bool mbar_try_wait_sleep(uint64_t *bar, uint32_t phase, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, "
+      "p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Non-blocking probe: has the phase with this parity completed?
 OSCAR_DEVINL bool mbar_test(uint64_t *bar, uint32_t phase) {
   uint32_t ok;

@@ -35,10 +35,13 @@
 // the four heads of a token row are fetched together.  Warp roles:
 //   0-3   softmax (thread = TMEM lane = token): scores, lazy max, P', l, zp; item epilogue
 //   4-7   key operands (thread = token = TMEM lane)
-//   8-11  value operands (lane = one code word of one token; conflict-free loads/stores)
-//   12    producer (lane 0: TMA copies into a 5-stage ring)
-//   13    MMA issuer (lane 0), tensor-memory allocation
-//   14    query operands (double buffered, one item ahead) and the -inf marks of unused splits
+//   8-9   value operands (lane = one code word of one token; conflict-free loads/stores)
+//   10    producer (lane 0: TMA copies into a 5-stage ring)
+//   11    query operands (double buffered, one item ahead) and the -inf marks of unused splits
+//   12-15 MMA issuers, one per KV head of the CTA (lane 0), one per SM sub-partition: a
+//         small tcgen05.mma keeps its issuing thread busy for tens of cycles, and four
+//         issuers working at once raise the rate about fourfold (measured on B200).
+//         Each polls its head's score and value streams and issues whichever is ready.
 // Tensor memory: key A operand x2 (256 columns), scores x2 (32), O^T per head (2 M
 // tiles x 16 columns), and each softmax thread's running l / zp per head (16 columns
 // per head, loaded and stored with the scores of every tile instead of held in registers).  Every mbarrier wait is bounded; a timeout raises a CTA abort
@@ -60,9 +63,10 @@ constexpr int kF8Rows = 8;         // query rows per KV head (padded)
 constexpr int kF8N = 2 * kF8Rows;  // MMA N: rows x {hi, lo} part
 constexpr int kF8MaxHeads = 4;
 constexpr int kF8MaxTasks = 1024;
-constexpr int kF8Warps = 15;
+constexpr int kF8Warps = 16;  // 4 per SM sub-partition: 128 registers per thread
 constexpr int kF8Threads = 32 * kF8Warps;
-constexpr int kWarpKey0 = 4, kWarpVal0 = 8, kWarpProd = 12, kWarpMma = 13, kWarpQ = 14;
+constexpr int kWarpKey0 = 4, kWarpVal0 = 8, kWarpProd = 10, kWarpQ = 11, kWarpMma0 = 12;
+constexpr int kValWarps = kWarpProd - kWarpVal0;
 constexpr float kF8Slack = 4.f;   // re-base when a logit passes the running max by 2^4
 constexpr float kF8Offset = 4.f;  // P' = 2^(x - (m - 4)) <= 2^8 right after a re-base
 
@@ -87,8 +91,13 @@ constexpr int kOffSmall = kOffTok + 2 * kF8Tile * 16;
 
 struct F8Small {
   uint64_t full[kF8Stages], empty[kF8Stages];
-  uint64_t akey[2], sfull[2], sempty[2], vfull[2], pfull[2], vdone[2];
-  uint64_t qfull[2], qempty[2], ofree, mmadone;
+  // per-tile barriers, set t % 4, phase t / 4: one issuer's tiles of a set are consecutive
+  // phases, and every wait on another tile's set is at most one phase behind (its previous
+  // phase was already waited on), so parity waits are never ambiguous
+  uint64_t akey[4], sfull[4], sempty[4], vfull[4], pfull[4], vdone[4];
+  uint64_t qfull[2], qempty[2], ofree;
+  uint64_t hvdone[kF8MaxHeads];  // phase k: the k-th value MMA group of head h has completed
+  uint64_t mmadone[kF8MaxHeads];
   float qfac[2][kF8MaxHeads][kF8Rows];
   float mrun[kF8MaxHeads][kF8Rows];
   float wmax[4][kF8Rows];
@@ -101,7 +110,7 @@ struct F8Small {
   int32_t n_items;
   int32_t pref[kF8MaxTasks + 1];
 };
-constexpr int kF8Smem = kOffSmall + (int)sizeof(F8Small) + 1024;
+constexpr int kF8Smem = kOffSmall + (int)sizeof(F8Small);
 static_assert(kF8Smem <= 227 * 1024, "shared memory budget");
 static_assert(kColL + kF8MaxHeads * 2 * kF8Rows <= kTmemCols, "tensor memory budget");
 
@@ -121,12 +130,15 @@ struct F8Item {
 
 OSCAR_DEVINL volatile int32_t &abort_word(F8Small &S) { return *reinterpret_cast<volatile int32_t *>(&S.abort); }
 
-// Bounded wait on an mbarrier phase.  Gives up at the probe limit (raising the CTA abort
-// flag and the status word) or as soon as another role has raised the flag.
+// Bounded wait on an mbarrier phase.  Each probe may suspend the thread for up to 4 us
+// (it wakes when the phase completes), so waiting warps do not spin; the wait gives up at
+// the probe limit (about 4 s at the default), raising the CTA abort flag and the status
+// word, or as soon as another role has raised the flag.
+constexpr uint32_t kF8ProbeNs = 4000;
 OSCAR_DEVINL bool f8_wait(uint64_t *bar, uint32_t parity, F8Small &S, const F8Params &T) {
   for (uint32_t i = 0; i < T.wait_probes; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 63u && abort_word(S) != 0) return false;
+    if (mbar_try_wait_sleep(bar, parity, kF8ProbeNs)) return true;
+    if ((i & 7u) == 7u && abort_word(S) != 0) return false;
   }
   atomicExch(&S.abort, 1);
   if (T.P.status) atomicExch(T.P.status, OSCAR_ERR_TIMEOUT);
@@ -225,6 +237,38 @@ OSCAR_DEVINL int64_t f8_out_row(const F8Item &it, const oscar_geometry &g, int H
   return ((int64_t)tok * g.kv_heads * g.group + qh) * split_slots + it.split;
 }
 
+// Walks this CTA's tiles of one KV head in order: items blockIdx.x, blockIdx.x +
+// gridDim.x, ... that have blocks, each nblk blocks x HG heads (head fastest).  t is the
+// CTA-wide tile index, i the tile index within the item, kq the ordinal of the item.
+struct F8Cursor {
+  int j, kq, ntile, i, t;
+  bool done;
+  OSCAR_DEVINL void seek(const F8Params &T, const F8Small &S, int n_items, int HG) {
+    while (j < n_items) {
+      const F8Item it = f8_item(T, S, j, HG);
+      if (it.nblk > 0) {
+        ntile = it.nblk * HG;
+        return;
+      }
+      j += gridDim.x;
+    }
+    done = true;
+  }
+  OSCAR_DEVINL void start(const F8Params &T, const F8Small &S, int n_items, int HG, int head) {
+    j = blockIdx.x, kq = 0, ntile = 0, i = head, t = head, done = false;
+    seek(T, S, n_items, HG);
+  }
+  OSCAR_DEVINL void next(const F8Params &T, const F8Small &S, int n_items, int HG, int head) {
+    t += HG;
+    i += HG;
+    if (i < ntile) return;
+    ++kq;
+    i = head;
+    j += gridDim.x;
+    seek(T, S, n_items, HG);
+  }
+};
+
 // The token's two e4m3 tables of its four bf16 key levels (bytes c = level c) and the
 // power of two that undoes their scale.  Invalid tokens get zero tables.
 OSCAR_DEVINL void key_tables(uint32_t ksz, bool valid, uint32_t &thi, uint32_t &tlo, float &tokfac) {
@@ -256,8 +300,9 @@ OSCAR_DEVINL float vt_fac(int m) { return ((m >> 2) & 1) ? 128.f : 512.f; }
 // ---------------------------------------------------------------------------------
 template <int HG>
 __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_constant__ F8Params T) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // used directly (no integer round trip for alignment), so the compiler keeps every
+  // access in the shared address space; no layout here needs more than 128-byte alignment
+  extern __shared__ __align__(128) uint8_t smem[];
   F8Small &S = *reinterpret_cast<F8Small *>(smem + kOffSmall);
   const HistParams &P = T.P;
   const oscar_geometry &g = P.geo;
@@ -266,20 +311,26 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
   if (tid == 0) {
     for (int s = 0; s < kF8Stages; ++s) {
       mbar_init(&S.full[s], 1);
-      mbar_init(&S.empty[s], 8);  // 4 key + 4 value warps
+      mbar_init(&S.empty[s], 4 + kValWarps);  // key + value warps
     }
     for (int b = 0; b < 2; ++b) {
+
+      mbar_init(&S.qfull[b], 1);
+      mbar_init(&S.qempty[b], HG + 4);  // each issuer's last score MMA of the item + 4 softmax warps
+    }
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&S.akey[b], 4);
       mbar_init(&S.sfull[b], 1);
       mbar_init(&S.sempty[b], 4);
-      mbar_init(&S.vfull[b], 4);
+      mbar_init(&S.vfull[b], kValWarps);
       mbar_init(&S.pfull[b], 4);
       mbar_init(&S.vdone[b], 1);
-      mbar_init(&S.qfull[b], 1);
-      mbar_init(&S.qempty[b], 1 + 4);  // key MMAs of the item done + 4 softmax warps past it
     }
     mbar_init(&S.ofree, 4);
-    mbar_init(&S.mmadone, 1);
+    for (int h = 0; h < kF8MaxHeads; ++h) {
+      mbar_init(&S.hvdone[h], 1);
+      mbar_init(&S.mmadone[h], 1);
+    }
     S.abort = 0;
     fence_mbarrier_init();
   }
@@ -326,7 +377,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
       S.n_items = nt * P.splits * T.nhg;
     }
   }
-  if (warp == kWarpMma) tmem_alloc(&S.tmem, kTmemCols);
+  if (warp == kWarpMma0) tmem_alloc(&S.tmem, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -363,70 +414,80 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
       for (int u = max(0, t - kF8Stages); u < t; ++u)
         if (!(blockIdx.x == 0 && u == T.withhold_tile)) f8_drain(&S.full[u % kF8Stages], (u / kF8Stages) & 1, T.wait_probes);
     }
-  } else if (warp == kWarpMma) {
-    // ===================== MMA issuer =====================
-    if (lane == 0) {
+  } else if (warp >= kWarpMma0) {
+    // ===================== MMA issuers: one per KV head =====================
+    // Issuer h handles the tiles of head h.  Scores (16 MMAs of tile t) need A(t) and the
+    // S buffer back from the softmax of tile t - 2; values (8 MMAs of tile t) need P'(t),
+    // V^T(t) and, on an item's first block, the O columns back from the last epilogue.
+    // The two streams are polled, never waited on one after the other.
+    const int hi = warp - kWarpMma0;
+    if (lane == 0 && hi < HG) {
       const uint32_t idk = idesc_e4m3_m128(kF8N, false, false);
       const uint32_t idv = idesc_e4m3_m128(kF8N, true, true);
-      int t = 0, kq = 0;
-      bool ok = true;
-      int pv_t = -1, pv_h = 0, pv_kq = 0;
-      bool pv_first = false;
-      auto issue_v = [&](int u, int hu, bool first, int ku) -> bool {
-        if (first && hu == 0 && ku >= 1 && !f8_wait(&S.ofree, (ku - 1) & 1, S, T)) return false;
-        const int a = u & 1;
-        if (!f8_wait(&S.pfull[a], (u >> 1) & 1, S, T) || !f8_wait(&S.vfull[a], (u >> 1) & 1, S, T)) return false;
-        tc_fence_after();
-        const uint32_t pb = smem_u32(smem + kOffP + a * kPBufBytes);
+      F8Cursor kc, vc;
+      kc.start(T, S, n_items, HG, hi);
+      vc.start(T, S, n_items, HG, hi);
+      uint32_t idle = 0;
+      const uint32_t idle_limit = T.wait_probes * 8u;  // backed-off polls, a few seconds at the default limit
+      while (!vc.done) {
+        bool did = false;
+        if (!kc.done) {
+          const int t = kc.t, a = t & 1;
+          if (mbar_test(&S.akey[t & 3], (t >> 2) & 1) && (t < 2 || mbar_test(&S.sempty[(t - 2) & 3], ((t - 2) >> 2) & 1)) &&
+              (kc.i >= HG || mbar_test(&S.qfull[kc.kq & 1], (kc.kq >> 1) & 1))) {
+            tc_fence_after();
+            const uint32_t d = tmem + kColS + (uint32_t)(a * kF8N);
+            const uint32_t at = tmem + kColA + (uint32_t)(a * 128);
+            // the start-address field (bits 0-13, 16-byte units) advances by 32 per 32-byte
+            // K step; the other fields of a descriptor are fixed
+            const uint64_t qd =
+                smem_desc_plain(smem_u32(smem + kOffQ + (kc.kq & 1) * kQBufBytes + hi * kQHeadBytes), kF8N * 16, 128);
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          const uint32_t d = tmem + kColO + (uint32_t)((hu * 2 + mt) * kF8N);
-          const uint32_t vt = smem_u32(smem + kOffVt + a * kVtBufBytes + mt * kVtTileBytes);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f8(d, smem_desc_plain(vt + 512 * k, 128, kVtSbo), smem_desc_plain(pb + 512 * k, 128, 2048), idv,
-                    (first && k == 0) ? 0u : 1u);
+            for (int k = 0; k < 16; ++k) umma_f8_ts(d, at + 8 * k, qd + (uint64_t)(32 * (k & 7)), idk, k > 0 ? 1u : 0u);
+            umma_commit(&S.sfull[t & 3]);
+            if (kc.i >= kc.ntile - HG) umma_commit(&S.qempty[kc.kq & 1]);
+            kc.next(T, S, n_items, HG, hi);
+            did = true;
+          }
         }
-        umma_commit(&S.vdone[a]);
-        return true;
-      };
-      for (int j = blockIdx.x; j < n_items && ok; j += step) {
-        const F8Item it = f8_item(T, S, j, HG);
-        if (it.nblk <= 0) continue;
-        const int qb = kq & 1;
-        if (!f8_wait(&S.qfull[qb], (kq >> 1) & 1, S, T)) {
-          ok = false;
+        if (vc.t < kc.t) {
+          const int t = vc.t, a = t & 1;
+          const bool first = vc.i < HG;
+          if ((!first || vc.kq == 0 || mbar_test(&S.ofree, (vc.kq - 1) & 1)) && mbar_test(&S.pfull[t & 3], (t >> 2) & 1) &&
+              mbar_test(&S.vfull[t & 3], (t >> 2) & 1)) {
+            tc_fence_after();
+            const uint64_t pd = smem_desc_plain(smem_u32(smem + kOffP + a * kPBufBytes), 128, 2048);
+            const uint64_t vd = smem_desc_plain(smem_u32(smem + kOffVt + a * kVtBufBytes), 128, kVtSbo);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+              const uint32_t d = tmem + kColO + (uint32_t)((hi * 2 + mt) * kF8N);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma_f8(d, vd + (uint64_t)(mt * (kVtTileBytes >> 4) + 32 * k), pd + (uint64_t)(32 * k), idv,
+                        (first && k == 0) ? 0u : 1u);
+            }
+            umma_commit(&S.vdone[t & 3]);
+            umma_commit(&S.hvdone[hi]);
+            vc.next(T, S, n_items, HG, hi);
+            did = true;
+          }
+        }
+        if (did) {
+          idle = 0;
+        } else if (++idle >= idle_limit) {
+          atomicExch(&S.abort, 1);
+          if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
           break;
+        } else if ((idle & 63u) == 0u && abort_word(S) != 0) {
+          break;
+        } else {
+          // nothing ready: back off, so the polling thread does not take issue slots from
+          // the softmax and key warps of its sub-partition
+          __nanosleep(idle < 4 ? 32u : (idle < 16 ? 128u : 512u));
         }
-        const uint32_t qbase = smem_u32(smem + kOffQ + qb * kQBufBytes);
-        const int ntile = it.nblk * HG;
-        for (int i = 0; i < ntile; ++i, ++t) {
-          const int h = i % HG, a = t & 1;
-          if (!f8_wait(&S.akey[a], (t >> 1) & 1, S, T) ||
-              (t >= 2 && !f8_wait(&S.sempty[a], ((t >> 1) - 1) & 1, S, T))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + kColS + (uint32_t)(a * kF8N);
-          const uint32_t at = tmem + kColA + (uint32_t)(a * 128);
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            umma_f8_ts(d, at + 8 * k, smem_desc_plain(qbase + h * kQHeadBytes + (k & 7) * 512, kF8N * 16, 128), idk,
-                       k > 0 ? 1u : 0u);
-          umma_commit(&S.sfull[a]);
-          if (i == ntile - 1) umma_commit(&S.qempty[qb]);
-          if (pv_t >= 0 && !issue_v(pv_t, pv_h, pv_first, pv_kq)) {
-            ok = false;
-            break;
-          }
-          pv_t = t, pv_h = h, pv_first = i < HG, pv_kq = kq;
-        }
-        ++kq;
       }
-      if (ok && pv_t >= 0) issue_v(pv_t, pv_h, pv_first, pv_kq);
-      umma_commit(&S.mmadone);
-      f8_drain(&S.mmadone, 0, T.wait_probes);  // all issued MMAs complete before teardown
+      umma_commit(&S.mmadone[hi]);
+      f8_drain(&S.mmadone[hi], 0, T.wait_probes);  // this issuer's MMAs complete before teardown
     }
   } else if (warp == kWarpQ) {
     // ===================== query operands (+ unused-split marks) =====================
@@ -523,14 +584,9 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
             break;
           }
           const uint8_t *row = smem + kOffStage + s * kF8StageBytes + tau * kF8Slot;
-          uint4 kc[4];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) kc[c] = *reinterpret_cast<const uint4 *>(row + 16 * c);
           const uint32_t ksz = *reinterpret_cast<const uint32_t *>(row + 64);
           const uint32_t vsz = *reinterpret_cast<const uint32_t *>(row + 132);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&S.empty[s]);
-          if (t >= 2 && !f8_warp_wait(&S.sempty[a], ((t >> 1) - 1) & 1, S, T)) {
+          if (t >= 2 && !f8_warp_wait(&S.sempty[(t - 2) & 3], ((t - 2) >> 2) & 1, S, T)) {
             ok = false;
             break;
           }
@@ -546,10 +602,13 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
           info.z = rvs;
           info.w = valid ? vz * rvs : 0.f;
           tokbuf[a * kF8Tile + tau] = info;
-#pragma unroll
+          // the codes are read group by group (a compact loop), so the stage is released
+          // after the last group
+#pragma unroll 1
           for (int grp = 0; grp < 4; ++grp) {
             uint32_t hv[16], lv[16];
-            const uint32_t kw[4] = {kc[grp].x, kc[grp].y, kc[grp].z, kc[grp].w};
+            const uint4 kq4 = *reinterpret_cast<const uint4 *>(row + 16 * grp);
+            const uint32_t kw[4] = {kq4.x, kq4.y, kq4.z, kq4.w};
 #pragma unroll
             for (int w2 = 0; w2 < 4; ++w2) {
               const uint32_t x = kw[w2];
@@ -563,21 +622,23 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
             tmem_store16(lane_base + kColA + (uint32_t)(a * 128 + 16 * grp), hv);
             tmem_store16(lane_base + kColA + (uint32_t)(a * 128 + 64 + 16 * grp), lv);
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.empty[s]);
           tmem_store_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&S.akey[a]);
+          if (lane == 0) mbar_arrive(&S.akey[t & 3]);
         }
       }
     }
   } else if (warp >= kWarpVal0 && warp < kWarpProd) {
     // ===================== value operands: V^T tile in shared memory =====================
-    // lane = (token, code word): rounds of 8 tokens; warp wv takes tokens
-    // {4(wv>>1) + (wv&1), +2} of each round, so the two tokens of one load are 320 bytes
-    // apart and the 32 loads hit 32 distinct banks
+    // lane = (token, code word): rounds of 4 tokens; warp wv takes tokens {wv, wv + 2}
+    // of each round, so the two tokens of one load are 320 bytes apart and the 32 loads
+    // hit 32 distinct banks
     const int wv = warp - kWarpVal0;
     const int word = lane & 15;
-    const int tok_off = 4 * (wv >> 1) + (wv & 1) + 2 * (lane >> 4);
+    const int tok_off = wv + 2 * (lane >> 4);
     int t = 0;
     bool ok = true;
     for (int j = blockIdx.x; j < n_items && ok; j += step) {
@@ -590,26 +651,31 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
           ok = false;
           break;
         }
-        const uint8_t *src = smem + kOffStage + s * kF8StageBytes + 68 + 4 * word;
-        uint32_t x[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) x[r] = *reinterpret_cast<const uint32_t *>(src + (8 * r + tok_off) * kF8Slot);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[s]);
-        if (t >= 2 && !f8_warp_wait(&S.vdone[a], ((t >> 1) - 1) & 1, S, T)) {
+        if (t >= 2 && !f8_warp_wait(&S.vdone[(t - 2) & 3], ((t - 2) >> 2) & 1, S, T)) {
           ok = false;
           break;
         }
+        const uint8_t *src = smem + kOffStage + s * kF8StageBytes + 68 + 4 * word;
         uint8_t *dst = smem + kOffVt + a * kVtBufBytes + (word >> 3) * kVtTileBytes + (word & 7) * kVtSbo;
+        // four chunks of 8 rounds (a compact loop); the stage is released after the last
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {
+          uint32_t x[8];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          const uint32_t xs = x[r] >> 4;
-          *reinterpret_cast<uint4 *>(dst + (8 * r + tok_off) * 16) =
-              make_uint4(x[r] & 0x03030303u, x[r] & 0x0C0C0C0Cu, xs & 0x03030303u, xs & 0x0C0C0C0Cu);
+          for (int r = 0; r < 8; ++r)
+            x[r] = *reinterpret_cast<const uint32_t *>(src + (4 * (r0 + r) + tok_off) * kF8Slot);
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const uint32_t xs = x[r] >> 4;
+            *reinterpret_cast<uint4 *>(dst + (4 * (r0 + r) + tok_off) * 16) =
+                make_uint4(x[r] & 0x03030303u, x[r] & 0x0C0C0C0Cu, xs & 0x03030303u, xs & 0x0C0C0C0Cu);
+          }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[s]);
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.vfull[a]);
+        if (lane == 0) mbar_arrive(&S.vfull[t & 3]);
       }
     }
   } else {
@@ -622,6 +688,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
     const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
     const float4 *tokbuf = reinterpret_cast<const float4 *>(smem + kOffTok);
     int t = 0, kq = 0, vc = 0;
+    int blocks_done = 0;  // blocks of every item before the current one and of this item so far
     bool ok = true, stop = false;
     int jfail = n_items;
     // all four warps: returns the OR of their `bits` (bit 0: failed wait, bit 1: re-base)
@@ -654,12 +721,13 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
 #pragma unroll
         for (int h = 0; h < HG; ++h) tmem_store16(lane_base + kColL + (uint32_t)(16 * h), zero);
       }
-      for (int b = 0; b < it.nblk && !stop; ++b) {
-#pragma unroll
+      const int item_blocks0 = blocks_done;
+      for (int b = 0; b < it.nblk && !stop; ++b, ++blocks_done) {
+#pragma unroll 1
         for (int h = 0; h < HG; ++h) {
           if (stop) break;
           const int a = t & 1;
-          if (ok && (!f8_warp_wait(&S.akey[a], (t >> 1) & 1, S, T) || !f8_warp_wait(&S.sfull[a], (t >> 1) & 1, S, T)))
+          if (ok && (!f8_warp_wait(&S.akey[t & 3], (t >> 2) & 1, S, T) || !f8_warp_wait(&S.sfull[t & 3], (t >> 2) & 1, S, T)))
             ok = false;
           float lg[kF8Rows], m[kF8Rows];
           float4 info = make_float4(0.f, -INFINITY, 0.f, 0.f);
@@ -673,7 +741,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
             info = tokbuf[a * kF8Tile + tau];
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S.sempty[a]);
+            if (lane == 0) mbar_arrive(&S.sempty[t & 3]);
 #pragma unroll
             for (int r = 0; r < kF8Rows; ++r) {
               const float dot = __uint_as_float(sv[r]) + __uint_as_float(sv[kF8Rows + r]);
@@ -714,8 +782,11 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
               m[r] = mn;
             }
             if (resc) {
-              // every earlier value MMA (this head's included) completes before O is re-based in place
-              if (t >= 1 && !f8_warp_wait(&S.vdone[(t - 1) & 1], ((t - 1) >> 1) & 1, S, T)) ok = false;
+              // the head's earlier value MMAs complete before its O columns are re-based in
+              // place (m was finite, so this item has an earlier block of head h)
+              if (blocks_done > item_blocks0 &&
+                  !f8_warp_wait(&S.hvdone[h], (blocks_done - 1) & 1, S, T))
+                ok = false;
               if (ok) {
                 tc_fence_after();
 #pragma unroll
@@ -761,14 +832,14 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
             lw[r >> 2] |= el << (16 * ((r >> 1) & 1));
           }
           if (ok) tmem_store16(lane_base + kColL + (uint32_t)(16 * h), lz);
-          if (ok && t >= 2 && !f8_warp_wait(&S.vdone[a], ((t >> 1) - 1) & 1, S, T)) ok = false;
+          if (ok && t >= 2 && !f8_warp_wait(&S.vdone[(t - 2) & 3], ((t - 2) >> 2) & 1, S, T)) ok = false;
           if (ok) {
             *reinterpret_cast<uint4 *>(smem + kOffP + a * kPBufBytes + tau * 16) =
                 make_uint4(hw[0], hw[1], lw[0], lw[1]);
             fence_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S.pfull[a]);
+            if (lane == 0) mbar_arrive(&S.pfull[t & 3]);
           }
           ++t;
         }
@@ -779,7 +850,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
       }
       // ---- item epilogue: row sums over the 128 token lanes, O^T -> partials ----
       tmem_store_wait();
-#pragma unroll
+#pragma unroll 1
       for (int h = 0; h < HG; ++h) {
         uint32_t lzh[16];
         tmem_load16(lane_base + kColL + (uint32_t)(16 * h), lzh);
@@ -794,8 +865,9 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
           if (lane == 0) S.red[warp][h][r][0] = lv, S.red[warp][h][r][1] = zv;
         }
       }
-      // the item's last value MMA (and with it every earlier one)
-      if (ok && !f8_warp_wait(&S.vdone[(t - 1) & 1], ((t - 1) >> 1) & 1, S, T)) ok = false;
+      // every head's last value MMAs of the item
+      for (int h = 0; h < HG && ok; ++h)
+        if (!f8_warp_wait(&S.hvdone[h], (blocks_done - 1) & 1, S, T)) ok = false;
       if (vote(ok ? 0 : 1) & 1) {
         jfail = j;
         break;
@@ -809,7 +881,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
       named_sync128();
       const int d0 = vt_dim(tau, 0), d1 = vt_dim(tau, 1);
       const float fac = vt_fac(tau);
-#pragma unroll
+#pragma unroll 1
       for (int h = 0; h < HG; ++h) {
         uint32_t o0[16], o1[16];
         tmem_load16(lane_base + kColO + (uint32_t)((h * 2 + 0) * kF8N), o0);
@@ -857,7 +929,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) history_f8_kernel(const __grid_
   __syncwarp();  // lanes that skipped a lane-0 role rejoin before the block barrier
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) {
+  if (warp == kWarpMma0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }

@@ -1,7 +1,7 @@
 """The 8-bit tcgen05 decode history kernel (history_f8_kernel) against the CPU oracle.
 
-It serves every launch with at most 8 query rows per KV head (decode, and short MTP
-rows at small GQA groups).  Which kernel ran is asserted by name through the CUDA
+It covers launches with at most 8 query rows per KV head (decode, and short MTP rows at
+small GQA groups) and is selected with OSCAR_HISTORY_F8=1.  Which kernel ran is asserted by name through the CUDA
 profiler.  Tolerances as elsewhere: output atol .035 / rtol .04 and rel 1e-2 in norm
 (reference tests/test_npu_kernels.py:194), LSE within 1e-3 abs.
 """
@@ -19,6 +19,12 @@ from tests.helpers import Scenario, make_config
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 F8 = "history_f8_kernel"
+
+
+@pytest.fixture(autouse=True)
+def f8_selected(monkeypatch):
+    """The kernel is opt-in (OSCAR_HISTORY_F8=1, read at every launch)."""
+    monkeypatch.setenv("OSCAR_HISTORY_F8", "1")
 
 
 def rel_err(a, b):
