@@ -87,13 +87,15 @@ int oscar_version(void);
  * an error status, not a hang, and that the context stays usable. */
 int oscar_selftest_bounded_wait(int32_t *status, void *stream);
 
-/* Test hook for the timeout path of the decode history kernel (no counterpart in the
- * reference): from the next launch on, CTA 0 of the history kernel never issues the copy
- * of its tile `withhold_tile` (-1: none), and every device wait of that kernel gives up
- * after `wait_probes` probes (0: the default limit of 2^20).  The copy's consumers then
- * time out: the launch stores OSCAR_ERR_TIMEOUT into its status word, marks its rows
- * empty (lse -inf) and returns.  Process-wide; for tests only. */
-int oscar_test_set_wait_fault(int32_t withhold_tile, uint32_t wait_probes);
+/* Test hook for the timeout path of the decode history kernels (no counterpart in the
+ * reference): from the next launch on, CTA (0, 0, 0) of every history launch (the default
+ * mma.sync kernels and the opt-in tcgen05 kernel) never issues the copy of its chunk / tile
+ * `withhold` (-1: none), and every bounded device wait of those launches gives up after
+ * `wait_probes` probes (0: the default limit of 2^20).  The copy's consumers then time
+ * out: the launch stores OSCAR_ERR_TIMEOUT into its status word, marks the aborted CTA's
+ * rows empty (lse -inf), lets its issued copies land and returns.  Process-wide; for
+ * tests only. */
+int oscar_test_set_wait_fault(int32_t withhold, uint32_t wait_probes);
 
 /* Y[n,h,:] = bf16( bf16(X[n,h,:]) @ bf16(R) ), fp32 accumulation.
  * Replaces reference oscar_ascend/kernels.py:51-66 (rotate / _rotate_kernel). */

@@ -98,12 +98,14 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
   uint64_t *empty = full + STAGES;
   uint8_t *stages = smem + 128;
   __shared__ int32_t s_abort;  // any warp's wait gave up: the CTA's partials are not valid
+  __shared__ int32_t s_stage_chunk[STAGES];  // last chunk whose copy went into each stage
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], P.consumers);
     }
     s_abort = 0;
+    for (int s = 0; s < STAGES; ++s) s_stage_chunk[s] = -1;
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -121,7 +123,9 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
     const int64_t slot0 = (int64_t)trow[pos / kKernelBlock] * kKernelBlock + pos % kKernelBlock;
     const uint8_t *src = P.history + (slot0 / g.block_tokens) * g.page_bytes +
                          ((slot0 % g.block_tokens) * g.kv_heads + h0) * (int64_t)g.slot_bytes;
+    if (c == P.withhold && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) return;  // test hook
     const uint32_t dst = smem_u32(stages + s * P.stage_bytes);
+    s_stage_chunk[s] = c;
     mbar_arrive_expect_tx(&full[s], CT * token_bytes);
     if (hpc == g.kv_heads) {
       bulk_copy_g2s(dst, src, CT * token_bytes, &full[s]);
@@ -133,7 +137,6 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
   if (warp >= P.consumers) return;
   if (threadIdx.x == 0)
     for (int c = 0; c < min(STAGES - 1, nchunks); ++c) issue_one(c);
-  int last_issued = -1;
 
   // ---------------- consumer warps ----------------
   const int unit = warp % P.units, sub = warp / P.units;
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
 #pragma unroll 1
   for (int c = 0; c < nchunks && ok; ++c) {
     const int s = c % STAGES;
-    if (!mbar_wait_bounded(&full[s], (c / STAGES) & 1)) {
+    if (!mbar_wait_bounded(&full[s], (c / STAGES) & 1, P.wait_probes)) {
       ok = false;
       if (lane == 0) {
         atomicExch(&s_abort, 1);
@@ -329,13 +332,12 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
       const int cn = c + STAGES - 1;
       int good = 1;
       if (warp == c % P.consumers && lane == 0 && cn < nchunks) {
-        if (cn >= STAGES && !mbar_wait_bounded(&empty[cn % STAGES], ((cn / STAGES) - 1) & 1)) {
+        if (cn >= STAGES && !mbar_wait_bounded(&empty[cn % STAGES], ((cn / STAGES) - 1) & 1, P.wait_probes)) {
           good = 0;
           atomicExch(&s_abort, 1);
           if (P.status) atomicExch(P.status, OSCAR_ERR_TIMEOUT);
         } else {
           issue_one(cn);
-          last_issued = cn;
         }
       }
       if (!__shfl_sync(0xffffffffu, good, 0)) ok = false;
@@ -343,8 +345,6 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (!ok && lane == 0 && last_issued >= 0)
-    (void)mbar_wait_bounded(&full[last_issued % STAGES], (last_issued / STAGES) & 1);  // let it land
 
   // ---------------- combine the warps of a unit, write the partial ----------------
 #pragma unroll
@@ -358,6 +358,17 @@ __global__ void __launch_bounds__(32 * MAXW, MINB) history_attention_kernel(Hist
   }
   // every consumer warp is past its last stage read; reuse the stage ring
   asm volatile("bar.sync 1, %0;" ::"r"(P.consumers * 32));
+  if (*reinterpret_cast<volatile int32_t *>(&s_abort) != 0) {
+    // an aborted loop may leave copies in flight: no warp issues any more, so the last
+    // chunk copied into each stage is final; let those land before the ring is reused
+    // and the CTA exits
+    if (threadIdx.x == 0)
+      for (int s = 0; s < STAGES; ++s) {
+        const int cc = s_stage_chunk[s];
+        if (cc >= 0) (void)mbar_wait_bounded(&full[s], (cc / STAGES) & 1, P.wait_probes);
+      }
+    asm volatile("bar.sync 1, %0;" ::"r"(P.consumers * 32));
+  }
   // exchange area over the stage ring: one record (O^T fragment + running max) per
   // non-leader warp, then l / zp of every consumer warp
   float *xch = reinterpret_cast<float *>(stages);
@@ -1042,7 +1053,13 @@ static bool history_f8_enabled() {
   return v != nullptr && v[0] == '1';
 }
 
+// Test hook state (oscar_test_set_wait_fault), read at every history launch.
+static std::atomic<int32_t> g_withhold{-1};
+static std::atomic<uint32_t> g_wait_probes{kWaitLimit};
+
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {
+  P.withhold = g_withhold.load();
+  P.wait_probes = g_wait_probes.load();
   if (history_f8_enabled()) {
     const int rc = history_f8_launch(P, num_tasks, sm_count(), stream, priority);
     if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
@@ -1332,5 +1349,16 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
         vs1, reinterpret_cast<__nv_bfloat16 *>(window), qstarts, seq_lens, table, counts, geo);
     OSCAR_CHECK_LAUNCH();
   }
+  return OSCAR_OK;
+}
+
+// Test hook, no counterpart in the reference: CTA (0, 0, 0) of every later history launch
+// skips the copy of its chunk / tile `withhold` (-1: none) and every bounded device wait of
+// those launches gives up after `wait_probes` probes (0: the default limit).  The skipped
+// copy's consumers then time out, which exercises the timeout path (status word, -inf
+// rows, clean exit).
+extern "C" int oscar_test_set_wait_fault(int32_t withhold, uint32_t wait_probes) {
+  g_withhold.store(withhold < 0 ? -1 : withhold);
+  g_wait_probes.store(wait_probes == 0 ? kWaitLimit : wait_probes);
   return OSCAR_OK;
 }

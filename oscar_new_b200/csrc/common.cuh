@@ -182,8 +182,9 @@ OSCAR_DEVINL bool mbar_test(uint64_t *bar, uint32_t phase) {
 // Spin on an mbarrier phase with an iteration limit.  Returns false on timeout; the
 // caller records the error and stops consuming (never an unbounded hang).
 constexpr uint32_t kWaitLimit = 1u << 20;
-OSCAR_DEVINL bool mbar_wait_bounded(uint64_t *bar, uint32_t phase) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+OSCAR_DEVINL bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, uint32_t limit = kWaitLimit) {
+  if (limit == 0) limit = kWaitLimit;
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
   }
   return false;

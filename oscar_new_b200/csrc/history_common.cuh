@@ -39,6 +39,10 @@ struct HistParams {
   // total history * head groups / target_ctas); empty splits write only lse = -inf
   int32_t balanced;
   int32_t target_ctas;
+  // test hook (oscar_test_set_wait_fault): CTA 0 never issues the copy of this chunk / tile
+  // (-1: none); every bounded device wait gives up after wait_probes probes
+  int32_t withhold;
+  uint32_t wait_probes;
 };
 
 constexpr int kMinSplitTokens = 1024;

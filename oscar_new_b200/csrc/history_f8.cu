@@ -953,9 +953,6 @@ int launch_f8(F8Params &T, int grid, cudaStream_t stream, int priority) {
   return OSCAR_OK;
 }
 
-std::atomic<int32_t> g_withhold{-1};
-std::atomic<uint32_t> g_wait_probes{kWaitLimit};
-
 }  // namespace
 
 int history_f8_launch(const HistParams &P, int32_t num_tasks, int sm_count, cudaStream_t stream, int priority) {
@@ -970,8 +967,8 @@ int history_f8_launch(const HistParams &P, int32_t num_tasks, int sm_count, cuda
   memset(&T, 0, sizeof(T));
   T.P = P;
   T.nhg = g.kv_heads / hg;
-  T.withhold_tile = g_withhold.load();
-  T.wait_probes = g_wait_probes.load();
+  T.withhold_tile = P.withhold;
+  T.wait_probes = P.wait_probes;
   // work items per CTA: the balanced split span targets `target_ctas` items in all
   if (P.balanced) T.P.target_ctas = sm_count * 6;
   cuuint64_t dims[3] = {(cuuint64_t)g.kv_heads * kF8Slot, (cuuint64_t)g.block_tokens, (cuuint64_t)1 << 20};
@@ -992,15 +989,3 @@ int history_f8_launch(const HistParams &P, int32_t num_tasks, int sm_count, cuda
 }
 
 }  // namespace oscar
-
-using namespace oscar;
-
-// Test hook, no counterpart in the reference: make CTA 0 of every later history_f8
-// launch skip the copy of its tile `withhold_tile` (-1: none) and give every device wait
-// `wait_probes` probes (0: the default limit).  The skipped copy's consumers then time
-// out, which exercises the timeout path (status word, -inf rows, clean exit).
-extern "C" int oscar_test_set_wait_fault(int32_t withhold_tile, uint32_t wait_probes) {
-  g_withhold.store(withhold_tile < 0 ? -1 : withhold_tile);
-  g_wait_probes.store(wait_probes == 0 ? kWaitLimit : wait_probes);
-  return OSCAR_OK;
-}

@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
     const int64_t slot0 = (int64_t)trow[pos / kKernelBlock] * kKernelBlock + pos % kKernelBlock;
     const uint8_t *src = P.history + (slot0 / g.block_tokens) * g.page_bytes +
                          ((slot0 % g.block_tokens) * g.kv_heads + h0) * (int64_t)g.slot_bytes;
+    if (c == P.withhold && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) return;  // test hook
     const uint32_t dst = smem_u32(stages + s * P.stage_bytes);
     mbar_arrive_expect_tx(&full[s], kMtpChunk * token_bytes);
     if (hpc == g.kv_heads) {
@@ -133,7 +134,6 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
         bulk_copy_g2s(dst + tk * token_bytes, src + (int64_t)tk * g.kv_heads * g.slot_bytes, token_bytes, &full[s]);
     }
   };
-  int last_issued = -1;
   if (threadIdx.x == 0) {
     for (int c = 0; c < min(kMtpStages - 1, nchunks); ++c) issue_one(c);
     *next_issue = min(kMtpStages - 1, nchunks);
@@ -149,10 +149,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
       const int nx = *reinterpret_cast<volatile int32_t *>(next_issue);
       if (nx >= nchunks) return;
       if (nx >= kMtpStages && !mbar_test(&empty[nx % kMtpStages], ((nx / kMtpStages) - 1) & 1)) return;
-      if (atomicCAS(next_issue, nx, nx + 1) == nx) {
-        issue_one(nx);
-        last_issued = max(last_issued, nx);
-      }
+      if (atomicCAS(next_issue, nx, nx + 1) == nx) issue_one(nx);
     }
   };
 
@@ -201,7 +198,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
     uint32_t got = 0;
     if (lane == 0) {
 #pragma unroll 1
-      for (uint32_t it = 0; it < kWaitLimit; ++it) {
+      for (uint32_t it = 0, lim = P.wait_probes ? P.wait_probes : kWaitLimit; it < lim; ++it) {
         if (mbar_try_wait(&full[s], (c / kMtpStages) & 1)) {
           got = 1;
           break;
@@ -209,7 +206,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
         try_issue();
       }
     }
-    const bool have = __shfl_sync(0xffffffffu, got, 0) != 0 && mbar_wait_bounded(&full[s], (c / kMtpStages) & 1);
+    const bool have = __shfl_sync(0xffffffffu, got, 0) != 0 && mbar_wait_bounded(&full[s], (c / kMtpStages) & 1, P.wait_probes);
     if (!have) {
       if (lane == 0) {
         atomicExch(abort_word, 1);
@@ -382,8 +379,24 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
       try_issue();
     }
   }
-  if (!ok && lane == 0 && last_issued >= 0)
-    (void)mbar_wait_bounded(&full[last_issued % kMtpStages], (last_issued / kMtpStages) & 1);  // let it land
+  if (!ok && lane == 0) {
+    // Aborted: let the copies this warp may have issued land before it can exit.  This
+    // lane issues nothing more, so its chunks are below the claim counter `snap`; a chunk
+    // below snap - S has landed (the claim of snap - 1 needed every consumer past
+    // snap - 1 - S).  A chunk c also has landed once chunk c + S is claimed, which stops
+    // the wait before the stage's barrier can complete a second phase.
+    const int snap = *reinterpret_cast<volatile int32_t *>(next_issue);
+    const bool hooked = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+    const uint32_t lim = P.wait_probes ? P.wait_probes : kWaitLimit;
+    for (int cc = max(0, snap - kMtpStages); cc < snap; ++cc) {
+      if (hooked && cc == P.withhold) continue;
+#pragma unroll 1
+      for (uint32_t it = 0; it < lim; ++it)
+        if (mbar_try_wait(&full[cc % kMtpStages], (cc / kMtpStages) & 1) ||
+            *reinterpret_cast<volatile int32_t *>(next_issue) > cc + kMtpStages)
+          break;
+    }
+  }
 
   // ---------------- row sums over the head's warps, write the partials ----------------
   float *lz = reinterpret_cast<float *>(hs + L::lz);

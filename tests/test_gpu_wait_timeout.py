@@ -1,0 +1,55 @@
+"""The timeout path of the default decode history kernels on the GPU.
+
+With the test hook `oscar_test_set_wait_fault`, CTA (0, 0, 0) of the history launch never
+issues the copy of its second chunk and every bounded device wait gives up after 4096
+probes.  The launch must return, store OSCAR_ERR_TIMEOUT (4) in the status word, mark the
+aborted CTA's rows empty and leave the context usable: the next step, without the hook,
+matches the oracle with a clear status word.  Nothing here faults or hangs the GPU: the
+withheld copy is never issued, so only the waits run out.
+"""
+
+import pytest
+import torch
+
+from oscar_new_b200 import _lib, kernels
+from tests.helpers import Scenario, make_config
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.mark.parametrize(
+    "qlen,mtp,kernel",
+    [
+        ([1, 1], 0, "history_attention_kernel"),  # decode: GQA 6 x 4 KV heads, one row tile
+        ([4, 4], 3, "history_mtp_kernel"),  # MTP verify: 4 query tokens x GQA 6 = 3 row tiles
+    ],
+)
+def test_wait_timeout_reports_status_and_context_recovers(cuda_lib, monkeypatch, qlen, mtp, kernel):
+    monkeypatch.delenv("OSCAR_HISTORY_F8", raising=False)
+    sc = Scenario([1500, 2600], qlen, hq=24, h=4, cfg=make_config(4, 128, mtp), seed=93 + mtp)
+    n = sum(qlen)
+    q, k, v = sc.current()
+    sc.prepare_tasks()
+    rk, rv = sc.rk.to(DEV), sc.rv.to(DEV)
+    qrot = kernels.rotate_store(k, v, rk, rv, sc.history, sc.meta.slot_mapping, sc.meta.counts, sc.layout, query=q)
+    kernels.read_status(DEV)  # start from a clear word
+    out = torch.empty((n, 24 * 256), dtype=torch.bfloat16, device=DEV)
+    lib = _lib.lib()
+    assert lib.oscar_test_set_wait_fault(1, 4096) == 0
+    try:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            kernels.decode_attention(qrot, q, k, v, sc.history, sc.window, sc.meta, sc.layout, 1 / 16, 8, rv, out,
+                                     store_window=False)
+            torch.cuda.synchronize()
+    finally:
+        assert lib.oscar_test_set_wait_fault(-1, 0) == 0
+    status = kernels.read_status(DEV)
+    names = sorted({e.name for e in prof.events() if not e.name.startswith("cuda")})
+    assert any(kernel in nm for nm in names), names
+    assert status == 4
+    kernels.decode_attention(qrot, q, k, v, sc.history, sc.window, sc.meta, sc.layout, 1 / 16, 8, rv, out,
+                             store_window=False)
+    assert kernels.read_status(DEV) == 0
+    expect, _ = sc.expected()
+    torch.testing.assert_close(out.view(n, 24, 256).float().cpu(), expect, atol=0.035, rtol=0.04)
