@@ -132,6 +132,28 @@ int oscar_prepare_tasks(const int32_t *qstarts, const int32_t *counts, int32_t *
                         int64_t source_stride, int32_t *table, int64_t table_stride,
                         int32_t copy_columns, void *stream);
 
+/* Fixed per-step metadata arena (int32 words) that CUDA graphs read: words 0-1 the
+ * device counts [requests, active tokens], word 2 the task count, word 3 reserved; then,
+ * each 16-byte aligned, query starts [max_reqs + 1], sequence lengths [max_reqs], block
+ * table [max_reqs, columns] and task table [task_capacity, 2].  Writes the word offsets
+ * of {query starts, sequence lengths, block table, tasks, total words} to offsets[0..4].
+ * No reference counterpart: the reference keeps five separate device tensors
+ * (metadata.py:59-75). */
+int oscar_step_arena_layout(int32_t max_reqs, int32_t columns, int32_t task_capacity, int64_t *offsets);
+
+/* Stage one step's metadata into the arena in one launch: counts = {num_reqs,
+ * num_tokens}; query starts [0, num_reqs], sequence lengths [0, num_reqs); block-table
+ * columns [0, copy_columns) of rows [0, num_reqs) (source rows `table_stride` apart);
+ * slot_out[0, num_tokens) = slots; and the compact task table built from the source
+ * query starts.  num_reqs = num_tokens = 0 is the dummy / capture step: counts and task
+ * count become 0 and nothing else is touched.  Replaces the reference builder's copies,
+ * fills and prepare_tasks call (metadata.py:108-145, kernels.py:222-287). */
+int oscar_stage_step_metadata(const int32_t *qstarts, const int32_t *seq_lens, const int32_t *table,
+                              int64_t table_stride, const int64_t *slots, int32_t num_reqs,
+                              int32_t num_tokens, int32_t copy_columns, int32_t query_tile,
+                              int32_t *arena, int32_t max_reqs, int32_t columns, int32_t task_capacity,
+                              int64_t *slot_out, int64_t slot_capacity, void *stream);
+
 /* Split-KV paged attention partials, reference kernels.py:290-482 semantics.
  * raw = 0: INT2 history [sink_len, recent_begin) with rotated query; raw = 1: BF16
  * sink + recent (window) + causal current tokens with the unrotated query, 1 split.

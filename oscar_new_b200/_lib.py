@@ -57,6 +57,8 @@ _SIGNATURES = {
     "oscar_store_int2": [P, P, I64, P, P, P, Geometry, Clip, Clip, P],
     "oscar_rotate_store": [P, I64, I64, P, I64, I64, I64, P, P, P, P, P, Geometry, Clip, Clip, P, I64, I64, I32, P, P, P, P, P],
     "oscar_prepare_tasks": [P, P, P, P, I32, I32, I32, P, I64, P, I64, I32, P],
+    "oscar_step_arena_layout": [I32, I32, I32, P],
+    "oscar_stage_step_metadata": [P, P, P, I64, P, I32, I32, I32, I32, P, I32, I32, I32, P, I64, P],
     "oscar_attention_partials": [P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P, P],
     "oscar_merge_splits": [P, P, I64, I32, I32, P, P, P, P],
     "oscar_merge_paths": [P, P, P, I64, P, I64, I64, I32, P, P, P],

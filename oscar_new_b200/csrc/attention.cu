@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "history_common.cuh"
+#include "tasks.cuh"
 #include "rowgemm.cuh"
 
 namespace oscar {
@@ -924,8 +925,8 @@ __global__ void __launch_bounds__(256) window_store_kernel(const __nv_bfloat16 *
 }
 
 // ----------------------------------------------------------------------------
-// task table (reference _prepare_tasks_kernel): block 0 builds the table with a
-// block-wide scan; other blocks copy page-table columns.
+// task table (reference _prepare_tasks_kernel): block 0 builds the table (tasks.cuh);
+// other blocks copy page-table columns.
 // ----------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) prepare_tasks_kernel(const int32_t *__restrict__ qstarts,
                                                              const int32_t *__restrict__ counts,
@@ -944,49 +945,7 @@ __global__ void __launch_bounds__(1024) prepare_tasks_kernel(const int32_t *__re
     }
     return;
   }
-  __shared__ int32_t warp_sums[32];
-  __shared__ int32_t carry;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int base = 0; base < nr; base += blockDim.x) {
-    const int req = base + threadIdx.x;
-    int tiles = 0;
-    if (req < nr) {
-      const int s = min(qstarts[req], active), e = min(qstarts[req + 1], active);
-      tiles = (max(e - s, 0) + query_tile - 1) / query_tile;
-    }
-    int incl = tiles;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    if (lane == 31) warp_sums[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      int ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, ws, o);
-        if (lane >= o) ws += v;
-      }
-      warp_sums[lane] = ws;
-    }
-    __syncthreads();
-    const int excl = carry + (warp ? warp_sums[warp - 1] : 0) + incl - tiles;
-    for (int i = 0; i < tiles; ++i) {
-      const int slot = excl + i;
-      if (slot < capacity) {
-        tasks[2 * slot] = req;
-        tasks[2 * slot + 1] = i * query_tile;
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) carry += warp_sums[(blockDim.x >> 5) - 1];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) task_count[0] = min(carry, capacity);
+  build_task_table(qstarts, nr, active, tasks, task_count, capacity, query_tile);
 }
 
 // ----------------------------------------------------------------------------

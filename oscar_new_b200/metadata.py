@@ -1,11 +1,22 @@
-"""Graph-stable device metadata for the OSCAR backend, without device-to-host reads.
+"""Per-step device metadata of the OSCAR backend: vLLM's attention metadata builder.
 
-Mirrors the reference's ``oscar_ascend/metadata.py:36-170`` on vLLM's CUDA worker:
-fixed device buffers sized once (``max_num_seqs + 1`` requests, the batched-token
-budget plus the MTP tail, ``ceil(max_model_len/128) + r + 1`` table columns) so CUDA
-graphs replay with new contents; ``counts = [num_reqs, num_actual_tokens]`` bound every
-kernel on the device; a dummy / capture scope zeroes ``counts`` so recorded kernels
-touch no cache page.
+Contract kept from the reference builder (``oscar_ascend/metadata.py:36-170``):
+
+* capacities fixed at start-up so CUDA graphs replay with new contents: ``max_num_seqs + 1``
+  requests (graph padding may add a dummy row), the batched-token budget plus
+  ``(speculative + 4)`` tail slots per request, ``ceil(max_model_len / 128) +
+  blocks_per_page + 1`` block-table columns, and the task table those imply;
+* the device counts ``[requests, active tokens]`` bound every kernel, and a step built
+  inside :func:`dummy_run_scope` (graph capture, warm-up) stages zero counts, so its
+  recorded kernels touch no cache page;
+* steps with shared prefixes, non-causal attention, more requests / tokens / table
+  columns than the capacities, or metadata that is not on the GPU are refused.
+
+Structure here: the fixed metadata lives in ONE int32 arena on the device
+(``StepBuffers``; counts, task count, query starts, sequence lengths, block table, task
+table) plus one int64 slot buffer, and each step is staged by ONE native launch
+(``oscar_stage_step_metadata``) instead of separate copies, fills and a task-table
+kernel.  The builder never reads device memory on the host.
 """
 
 from __future__ import annotations
@@ -18,48 +29,120 @@ from dataclasses import dataclass
 import torch
 from vllm.v1.attention.backend import AttentionCGSupport, AttentionMetadataBuilder
 
+from . import kernels
 from .config import OscarConfig, task_capacity
 from .layout import CacheLayout
 
-_dummy = contextvars.ContextVar("oscar_dummy_run", default=False)
+_dummy_step = contextvars.ContextVar("oscar_dummy_step", default=False)
 
 
 @contextlib.contextmanager
 def dummy_run_scope(capturing: bool = False):
-    """Metadata built inside this scope owns no cache pages (reference startup.py:24-33)."""
-    token = _dummy.set(True)
+    """Steps built inside this scope own no cache pages (reference startup.py:24-33)."""
+    mark = _dummy_step.set(True)
     try:
         yield
     finally:
-        _dummy.reset(token)
+        _dummy_step.reset(mark)
 
 
 def in_dummy_run() -> bool:
-    return _dummy.get()
+    return _dummy_step.get()
 
 
-@dataclass
+@dataclass(frozen=True)
+class StepCapacity:
+    """Fixed sizes of one builder's device metadata."""
+
+    requests: int
+    tokens: int
+    columns: int
+    query_tile: int
+
+    @property
+    def tasks(self) -> int:
+        return task_capacity(self.tokens, self.requests, self.query_tile)
+
+    @classmethod
+    def for_engine(cls, vllm_config, layout: CacheLayout, cfg: OscarConfig) -> "StepCapacity":
+        requests = vllm_config.scheduler_config.max_num_seqs + 1
+        tail = (cfg.speculative_tokens + 4) * requests
+        columns = math.ceil(vllm_config.model_config.max_model_len / 128) + layout.blocks_per_page + 1
+        return cls(requests, vllm_config.scheduler_config.max_num_batched_tokens + tail, columns,
+                   cfg.queries_per_tile)
+
+
+class StepBuffers:
+    """The arena and slot buffer of one builder, with named views into the arena."""
+
+    def __init__(self, cap: StepCapacity, device):
+        self.cap = cap
+        off = kernels.step_arena_layout(cap.requests, cap.columns, cap.tasks)
+        self.arena = torch.zeros(off["words"], dtype=torch.int32, device=device)
+        self.slot_mapping = torch.full((cap.tokens,), -1, dtype=torch.int64, device=device)
+        a = self.arena
+        self.counts = a[0:2]
+        self.task_count = a[2:3]
+        self.query_start_loc = a[off["qstarts"]:off["qstarts"] + cap.requests + 1]
+        self.seq_lens = a[off["seq_lens"]:off["seq_lens"] + cap.requests]
+        self.block_tables = a[off["table"]:off["table"] + cap.requests * cap.columns].view(cap.requests, cap.columns)
+        self.tasks = a[off["tasks"]:off["tasks"] + 2 * cap.tasks].view(cap.tasks, 2)
+
+    def stage(self, source=None, num_reqs: int = 0, num_tokens: int = 0, copy_columns: int = 0):
+        """One launch: the step's counts, starts, lengths, reachable table columns, slots
+        and task table (``source`` None: a dummy step with zero counts)."""
+        c = self.cap
+        if source is None:
+            kernels.stage_step_metadata(self.arena, self.slot_mapping, c.requests, c.columns, c.tasks, c.query_tile)
+            return
+        kernels.stage_step_metadata(self.arena, self.slot_mapping, c.requests, c.columns, c.tasks, c.query_tile,
+                                    num_reqs=num_reqs, num_tokens=num_tokens, qstarts=source.query_start_loc,
+                                    seq_lens=source.seq_lens, table=source.block_table_tensor,
+                                    slots=source.slot_mapping, copy_columns=copy_columns)
+
+
+@dataclass(frozen=True)
 class OscarMetadata:
-    query_start_loc: torch.Tensor
-    seq_lens: torch.Tensor
-    block_tables: torch.Tensor
-    slot_mapping: torch.Tensor
-    counts: torch.Tensor
+    """One step's metadata: device views of the builder's buffers plus host scalars."""
+
+    buffers: StepBuffers
     num_reqs: int
     num_actual_tokens: int
     max_query_len: int
-    max_num_reqs: int
     layout: CacheLayout
-    causal: bool = True
     is_dummy: bool = False
-    tasks: torch.Tensor | None = None
-    task_count: torch.Tensor | None = None
-    # host-known first prefill: every request starts at position 0 (no history, no
-    # window yet); the forward then uses a library flash-attention kernel for the
-    # causal current-token attention (the reference hands this case to the vendor's
-    # fused attention, backend.py:175-193)
-    prefill_only: bool = False
-    query_start_loc_cpu: torch.Tensor | None = None
+    # host query starts when every request of the step is a first prefill (no history,
+    # no window yet); the forward then hands the causal attention to a library
+    # flash-attention kernel (the reference hands it to the vendor's fused attention,
+    # backend.py:175-193)
+    prefill_starts: torch.Tensor | None = None
+    causal: bool = True
+
+    query_start_loc = property(lambda self: self.buffers.query_start_loc)
+    seq_lens = property(lambda self: self.buffers.seq_lens)
+    block_tables = property(lambda self: self.buffers.block_tables)
+    slot_mapping = property(lambda self: self.buffers.slot_mapping)
+    counts = property(lambda self: self.buffers.counts)
+    tasks = property(lambda self: self.buffers.tasks)
+    task_count = property(lambda self: self.buffers.task_count)
+    max_num_reqs = property(lambda self: self.buffers.cap.requests)
+    prefill_only = property(lambda self: self.prefill_starts is not None)
+    query_start_loc_cpu = property(lambda self: self.prefill_starts)
+
+
+def _first_prefill_starts(cm, num_reqs: int):
+    """Host query starts if the scheduler's host data proves every request starts at
+    position 0, else None.  ``seq_lens_cpu_upper_bound`` is exact for prefill rows and
+    never below a true length, so bound == query length means an empty prefix; nothing
+    on the device is read."""
+    bound = getattr(cm, "seq_lens_cpu_upper_bound", None)
+    starts = getattr(cm, "query_start_loc_cpu", None)
+    if bound is None or starts is None or num_reqs == 0 or cm.max_query_len <= 16:
+        return None
+    starts = starts[: num_reqs + 1].to(torch.int64)
+    if torch.equal(bound[:num_reqs].to(torch.int64), starts[1:] - starts[:-1]):
+        return starts
+    return None
 
 
 class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
@@ -70,29 +153,23 @@ class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
         super().__init__(kv_cache_spec, layer_names, vllm_config, device)
         from .backend import OscarAttentionImpl
 
-        ctx = getattr(getattr(vllm_config, "compilation_config", None), "static_forward_context", None)
-        if ctx is not None:
-            for name in layer_names:
-                impl = getattr(ctx.get(name), "impl", None)
-                if impl is not None and not isinstance(impl, OscarAttentionImpl):
-                    raise TypeError(f"OSCAR implementation was replaced for {name}")
+        forward_ctx = getattr(getattr(vllm_config, "compilation_config", None), "static_forward_context", None) or {}
+        replaced = [n for n in layer_names
+                    if n in forward_ctx and not isinstance(getattr(forward_ctx[n], "impl", None), OscarAttentionImpl)]
+        if replaced:
+            raise TypeError(f"OSCAR attention implementation replaced on layers {replaced}")
         spec = vllm_config.speculative_config
         cfg = OscarConfig.from_env(spec.num_speculative_tokens if spec else 0)
-        self.query_tile = cfg.queries_per_tile
         self.layout = CacheLayout(kv_cache_spec.block_size, kv_cache_spec.num_kv_heads, config=cfg)
+        self.capacity = StepCapacity.for_engine(vllm_config, self.layout, cfg)
+        self.buffers = StepBuffers(self.capacity, device)
         self.reorder_batch_threshold = cfg.speculative_tokens + 1
-        sched = vllm_config.scheduler_config
-        self.max_reqs = sched.max_num_seqs + 1  # graph padding may add a dummy row
-        self.max_tokens = sched.max_num_batched_tokens + (cfg.speculative_tokens + 4) * self.max_reqs
-        cols = math.ceil(vllm_config.model_config.max_model_len / 128) + self.layout.blocks_per_page + 1
-        self.qstarts = torch.zeros(self.max_reqs + 1, dtype=torch.int32, device=device)
-        self.seqs = torch.zeros(self.max_reqs, dtype=torch.int32, device=device)
-        self.table = torch.zeros((self.max_reqs, cols), dtype=torch.int32, device=device)
-        self.slots = torch.full((self.max_tokens,), -1, dtype=torch.int64, device=device)
-        self.counts = torch.zeros(2, dtype=torch.int32, device=device)
-        self.tasks = torch.empty((task_capacity(self.max_tokens, self.max_reqs, self.query_tile), 2),
-                                 dtype=torch.int32, device=device)
-        self.task_count = torch.zeros(1, dtype=torch.int32, device=device)
+
+    # capacity views kept for callers that size their own inputs from the builder
+    max_reqs = property(lambda self: self.capacity.requests)
+    max_tokens = property(lambda self: self.capacity.tokens)
+    table = property(lambda self: self.buffers.block_tables)
+    counts = property(lambda self: self.buffers.counts)
 
     @classmethod
     def get_cudagraph_support(cls, vllm_config, kv_cache_spec):
@@ -101,52 +178,42 @@ class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
     def reorder_batch(self, input_batch, scheduler_output):
         return False
 
-    def build(self, common_prefix_len, common_attn_metadata, fast_build=False):
-        cm = common_attn_metadata
+    def _check(self, common_prefix_len, cm):
+        cap = self.capacity
         if common_prefix_len:
-            raise ValueError("Prefix sharing is unsupported by the request-owned BF16 ring")
+            raise ValueError("OSCAR keeps one BF16 ring per request: shared prefixes (cascade attention) "
+                             "are not supported")
         if not cm.causal:
-            raise ValueError("OSCAR supports causal decoder attention only")
-        nr, nt = cm.num_reqs, cm.num_actual_tokens
-        if nr > self.max_reqs or nt > self.max_tokens:
-            raise ValueError("OSCAR metadata capacity exceeded")
-        columns = cm.block_table_tensor.shape[1]
-        if columns > self.table.shape[1]:
-            raise ValueError("Native block table exceeds the configured OSCAR buffer")
+            raise ValueError("OSCAR implements causal decoder attention only")
+        if cm.num_reqs > cap.requests or cm.num_actual_tokens > cap.tokens:
+            raise ValueError(f"step of {cm.num_reqs} requests / {cm.num_actual_tokens} tokens is larger than "
+                             f"the metadata capacity ({cap.requests} / {cap.tokens})")
+        if cm.block_table_tensor.shape[1] > cap.columns:
+            raise ValueError(f"block table of {cm.block_table_tensor.shape[1]} columns is wider than the "
+                             f"{cap.columns} this builder holds")
         for name in ("query_start_loc", "seq_lens", "block_table_tensor", "slot_mapping"):
             if getattr(cm, name).device.type != "cuda":
-                raise ValueError(f"Expected CUDA metadata for {name}")
-        dummy = in_dummy_run()
-        copy_columns = 0
-        if dummy:
-            # A dummy/capture step owns no pages: zero counts mask every access on device.
-            self.counts.zero_()
-        else:
-            self.qstarts[: nr + 1].copy_(cm.query_start_loc[: nr + 1], non_blocking=True)
-            self.seqs[:nr].copy_(cm.seq_lens[:nr], non_blocking=True)
-            copy_columns = columns
-            max_seq_len = getattr(cm, "max_seq_len", None)
-            if isinstance(max_seq_len, int):
-                copy_columns = min(columns, max(1, -(-max_seq_len // self.layout.kernel_block_tokens)))
-            self.slots[:nt].copy_(cm.slot_mapping[:nt], non_blocking=True)
-            self.counts[0].fill_(nr)
-            self.counts[1].fill_(nt)
-        from .kernels import prepare_tasks
+                raise ValueError(f"{name} must be a CUDA tensor")
 
-        prepare_tasks(self.qstarts, self.counts, self.tasks, self.task_count, self.max_reqs, self.query_tile,
-                      source_table=cm.block_table_tensor, table=self.table, copy_columns=copy_columns)
-        prefill_only, qcpu = False, None
-        bound = getattr(cm, "seq_lens_cpu_upper_bound", None)
-        qcpu_src = getattr(cm, "query_start_loc_cpu", None)
-        if not dummy and bound is not None and qcpu_src is not None and nr > 0 and cm.max_query_len > 16:
-            # the bound is exact for prefill rows and never below the true length, so
-            # bound == query length proves a zero-length prefix
-            qcpu = qcpu_src[: nr + 1].to(torch.int64)
-            prefill_only = bool(torch.equal(bound[:nr].to(torch.int64), qcpu[1:] - qcpu[:-1]))
-        return OscarMetadata(self.qstarts, self.seqs, self.table, self.slots, self.counts, nr, nt,
-                             cm.max_query_len, self.max_reqs, self.layout, is_dummy=dummy, tasks=self.tasks,
-                             task_count=self.task_count, prefill_only=prefill_only,
-                             query_start_loc_cpu=qcpu if prefill_only else None)
+    def _reachable_columns(self, cm) -> int:
+        """Block-table columns a step can reach: all of them, or fewer when the host knows
+        the longest sequence (``max_seq_len``, a scheduler value, not a device read)."""
+        columns = cm.block_table_tensor.shape[1]
+        longest = getattr(cm, "max_seq_len", None)
+        if not isinstance(longest, int):
+            return columns
+        return min(columns, max(1, -(-longest // self.layout.kernel_block_tokens)))
+
+    def build(self, common_prefix_len, common_attn_metadata, fast_build=False):
+        cm = common_attn_metadata
+        self._check(common_prefix_len, cm)
+        if in_dummy_run():
+            self.buffers.stage()
+            return OscarMetadata(self.buffers, cm.num_reqs, cm.num_actual_tokens, cm.max_query_len, self.layout,
+                                 is_dummy=True)
+        self.buffers.stage(cm, cm.num_reqs, cm.num_actual_tokens, self._reachable_columns(cm))
+        return OscarMetadata(self.buffers, cm.num_reqs, cm.num_actual_tokens, cm.max_query_len, self.layout,
+                             prefill_starts=_first_prefill_starts(cm, cm.num_reqs))
 
     def build_for_cudagraph_capture(self, common_attn_metadata):
         with dummy_run_scope(capturing=True):

@@ -140,6 +140,44 @@ def test_three_dimensional_checkpoint(tmp_path):
     torch.testing.assert_close(get_rotation(str(path), "model.layers.1.attn", "cpu"), q.bfloat16())
 
 
+def test_rotation_file_is_checked_once_for_every_layer(tmp_path):
+    """All layers are audited when the file loads; a bad layer does not hide good ones."""
+    q, _ = torch.linalg.qr(torch.randn(256, 256, generator=torch.Generator().manual_seed(4)))
+    bad = q.clone()
+    bad[0, 0] = float("nan")
+    path = tmp_path / "mixed.pt"
+    torch.save({"layers": {0: {"rotation": q}, 1: bad, 2: torch.eye(128), 5: 2 * torch.eye(256)}}, path)
+    f = load_checkpoint(str(path))
+    assert sorted(f) == [0, 1, 2, 5] and set(f.problems) == {1, 5}
+    assert "non-finite" in f.problems[1] and "orthogonal" in f.problems[5]
+    torch.testing.assert_close(get_rotation(str(path), "model.layers.0.attn", "cpu"), q.bfloat16())
+    with pytest.raises(ValueError, match="non-finite"):
+        get_rotation(str(path), "model.layers.1.attn", "cpu")
+    torch.testing.assert_close(get_rotation(str(path), "model.layers.2.attn", "cpu", 128), torch.eye(128).bfloat16())
+    with pytest.raises(ValueError, match="D256"):
+        get_rotation(str(path), "model.layers.2.attn", "cpu")
+    with pytest.raises(ValueError, match="orthogonal"):
+        get_rotation(str(path), "model.layers.5.attn", "cpu")
+    with pytest.raises(ValueError, match="no decoder layer"):
+        get_rotation(str(path), "model.norm", "cpu")
+    torch.save({3: "not a matrix"}, tmp_path / "junk.pt")
+    with pytest.raises(ValueError, match="no rotation matrix"):
+        load_checkpoint(str(tmp_path / "junk.pt"))
+
+
+def test_step_arena_layout_segments_are_aligned_and_disjoint():
+    from oscar_new_b200.kernels import step_arena_layout
+
+    for reqs, cols, cap in ((5, 39, 19), (257, 262, 4096), (1, 1, 1)):
+        off = step_arena_layout(reqs, cols, cap)
+        assert off["qstarts"] == 4
+        ends = [off["qstarts"] + reqs + 1, off["seq_lens"] + reqs, off["table"] + reqs * cols,
+                off["tasks"] + 2 * cap]
+        starts = [off["qstarts"], off["seq_lens"], off["table"], off["tasks"]]
+        assert all(v % 4 == 0 for v in starts + [off["words"]])
+        assert all(e <= s for e, s in zip(ends, starts[1:] + [off["words"]]))
+
+
 # ----------------------------------------------------------------------------
 # backend / impl / plugin / builder
 # ----------------------------------------------------------------------------
@@ -283,7 +321,7 @@ def test_metadata_builder_sizes_and_rejections():
     assert OscarMetadataBuilder.get_cudagraph_support(None, None).name == "UNIFORM_BATCH"
     cm = SimpleNamespace(causal=True, num_reqs=1, num_actual_tokens=4, max_query_len=4,
                          block_table_tensor=torch.zeros(1, 6, dtype=torch.int32))
-    with pytest.raises(ValueError, match="Prefix"):
+    with pytest.raises(ValueError, match="shared prefixes"):
         b.build(16, cm)
     with pytest.raises(ValueError, match="causal"):
         b.build(0, SimpleNamespace(**{**vars(cm), "causal": False}))

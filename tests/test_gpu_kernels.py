@@ -307,6 +307,56 @@ def test_prepare_tasks_copies_table_columns(cuda_lib):
     assert (dst[3:] == -1).all() and (dst[:, 17:] == -1).all()
 
 
+def _stage(bufs_cap, **kw):
+    from oscar_new_b200.metadata import StepBuffers
+
+    bufs = StepBuffers(bufs_cap, DEV)
+    bufs.arena.fill_(-7)
+    bufs.slot_mapping.fill_(-9)
+    bufs.stage(**kw)
+    return bufs
+
+
+def test_stage_step_metadata_matches_reference_task_body(cuda_lib):
+    """One staging launch: counts, starts, lengths, reachable table columns, slots, and
+    the task table of the reference kernel body (golden fixture)."""
+    from types import SimpleNamespace
+
+    from oscar_new_b200.metadata import StepCapacity
+
+    for case in load("tasks.pt"):
+        nr, nt = int(case["counts"][0]), int(case["counts"][1])
+        cap = StepCapacity(requests=nr + 1, tokens=max(nt, 1) + 3, columns=23, query_tile=case["query_tile"])
+        assert cap.tasks >= case["count"]
+        g = torch.Generator().manual_seed(nr)
+        src = SimpleNamespace(query_start_loc=case["qstarts"][:nr + 1].to(DEV),
+                              seq_lens=torch.randint(1, 1 << 20, (nr,), generator=g, dtype=torch.int32).to(DEV),
+                              block_table_tensor=torch.randint(0, 1 << 30, (nr, 40), generator=g,
+                                                               dtype=torch.int32).to(DEV)[:, 3:31],
+                              slot_mapping=torch.randint(-1, 1 << 40, (nt,), generator=g).to(DEV))
+        b = _stage(cap, source=src, num_reqs=nr, num_tokens=nt, copy_columns=17)
+        assert b.counts.tolist() == [nr, nt]
+        assert torch.equal(b.query_start_loc[:nr + 1], src.query_start_loc)
+        assert torch.equal(b.seq_lens[:nr], src.seq_lens)
+        assert torch.equal(b.block_tables[:nr, :17], src.block_table_tensor[:, :17])
+        assert (b.block_tables[:, 17:] == -7).all() and (b.block_tables[nr:] == -7).all()
+        assert torch.equal(b.slot_mapping[:nt], src.slot_mapping)
+        assert (b.slot_mapping[nt:] == -9).all()
+        c = int(b.task_count.item())
+        assert c == case["count"]
+        assert torch.equal(b.tasks[:c].cpu(), case["tasks"][:c])
+        want, wc = oo.prepare_tasks(case["qstarts"], case["counts"], case["query_tile"], cap.tasks)
+        assert wc == c and torch.equal(b.tasks[:c].cpu(), want[:c])
+
+
+def test_stage_dummy_step_zeroes_counts_and_touches_nothing_else(cuda_lib):
+    from oscar_new_b200.metadata import StepCapacity
+
+    b = _stage(StepCapacity(requests=5, tokens=40, columns=9, query_tile=4))
+    assert b.counts.tolist() == [0, 0] and int(b.task_count.item()) == 0
+    assert (b.arena[3:] == -7).all() and (b.slot_mapping == -9).all()
+
+
 @pytest.mark.parametrize("seq,qlen", [([30, 70, 5], [20, 4, 5]), ([1500, 40, 700], [1200, 40, 3])])
 def test_store_windows_matches_oracle(cuda_lib, seq, qlen):
     """Sink and ring slots (latest writer only), short and prefill-sized chunks."""
