@@ -55,16 +55,19 @@ def decode_config():
             "sink": SINK, "recent": RECENT, "kv_splits": SPLITS, "page_tokens": BP}
 
 
-def workload_sizes():
+def workload_sizes(requests=None, kv_heads=None):
+    """Per-GPU sizes of a decode step of `requests` x `kv_heads` (default: config 3)."""
+    nr = B if requests is None else requests
+    h = H if kv_heads is None else kv_heads
     hist_tokens = SEQ - 1 - SINK - RECENT  # prefix minus sink and recent
-    hist_bytes = B * H * hist_tokens * HISTORY_BYTES_PER_TOKEN_HEAD
-    window_bytes = B * H * (SINK + RECENT) * 2 * D * 2
-    current = B * (H * G + 2 * H) * D * 2
-    out = B * H * G * D * 2
+    hist_bytes = nr * h * hist_tokens * HISTORY_BYTES_PER_TOKEN_HEAD
+    window_bytes = nr * h * (SINK + RECENT) * 2 * D * 2
+    current = nr * (h * G + 2 * h) * D * 2
+    out = nr * h * G * D * 2
     return dict(
-        kv_tokens=B * SEQ * H,
+        kv_tokens=nr * SEQ * h,
         history_bytes=hist_bytes,
-        footprint_bytes=B * H * hist_tokens * 160,
+        footprint_bytes=nr * h * hist_tokens * 160,
         algorithmic_bytes=hist_bytes + window_bytes + current + out,
     )
 
@@ -74,27 +77,31 @@ def workload_sizes():
 # ----------------------------------------------------------------------------
 
 
-def build_state(device, seed):
+def build_state(device, seed, requests=None, kv_heads=None):
+    """One GPU's share of the decode workload: `requests` x `kv_heads` (default config 3:
+    64 x 4), 32768-token contexts whose prefixes are written by the device store kernels."""
     from oscar_new_b200 import kernels
     from oscar_new_b200.config import OscarConfig
     from oscar_new_b200.layout import CacheLayout
     from oscar_new_b200.synthetic import cache_stripes, plan_pages, rotation
 
+    nr = B if requests is None else requests
+    h = H if kv_heads is None else kv_heads
     cfg = replace(OscarConfig(), sink_tokens=SINK, recent_tokens=RECENT, speculative_tokens=0)
-    layout = CacheLayout(BP, kv_heads=H, config=cfg)
-    plan = plan_pages([SEQ] * B, [1] * B, BP, seed=seed)
-    cache = cache_stripes(plan.num_pages, BP, H, device)
+    layout = CacheLayout(BP, kv_heads=h, config=cfg)
+    plan = plan_pages([SEQ] * nr, [1] * nr, BP, seed=seed)
+    cache = cache_stripes(plan.num_pages, BP, h, device)
     history, window = layout.tensor_views(cache)
     rk = rotation(1).bfloat16().to(device)
     rv = rotation(2).bfloat16().to(device)
     gen = torch.Generator(device=device).manual_seed(seed)
     prefix = SEQ - 1
     # fill every request's prefix with the device store kernels (history + window)
-    for req in range(B):
-        k = torch.randn(prefix, H, D, device=device, generator=gen)
+    for req in range(nr):
+        k = torch.randn(prefix, h, D, device=device, generator=gen)
         k[..., :8] *= 20
         k = k.bfloat16()
-        v = torch.randn(prefix, H, D, device=device, generator=gen).bfloat16()
+        v = torch.randn(prefix, h, D, device=device, generator=gen).bfloat16()
         slots = plan.slots_of(req, range(prefix)).to(device)
         counts = torch.tensor([1, prefix], dtype=torch.int32, device=device)
         kernels.rotate_store(k, v, rk, rv, history, slots, counts, layout)
@@ -107,18 +114,19 @@ def build_state(device, seed):
         kernels.store_windows(k, v, window, meta1, layout)
         del k, v
     meta = plan.meta(device, cfg.queries_per_tile)
-    q = torch.randn(B, H * G, D, device=device, generator=gen).bfloat16()
-    k = torch.randn(B, H, D, device=device, generator=gen)
+    q = torch.randn(nr, h * G, D, device=device, generator=gen).bfloat16()
+    k = torch.randn(nr, h, D, device=device, generator=gen)
     k[..., :8] *= 20
     k = k.bfloat16()
-    v = torch.randn(B, H, D, device=device, generator=gen).bfloat16()
+    v = torch.randn(nr, h, D, device=device, generator=gen).bfloat16()
     torch.cuda.synchronize(device)
     return dict(cfg=cfg, layout=layout, plan=plan, cache=cache, history=history, window=window, rk=rk, rv=rv,
-                meta=meta, q=q, k=k, v=v)
+                meta=meta, q=q, k=k, v=v, requests=nr, kv_heads=h)
 
 
 def layer_step(st, out, scratch):
-    """One drop-in layer forward (what OscarAttentionImpl.forward launches)."""
+    """One layer forward through the kernel wrappers (used for spot parity and ncu runs;
+    the timed legs go through OscarMetadataBuilder.build + OscarAttentionImpl.forward)."""
     from oscar_new_b200 import kernels
 
     m = st["meta"]
@@ -131,7 +139,59 @@ def layer_step(st, out, scratch):
     return qrot
 
 
-LAUNCHES_PER_STEP = 6  # tasks, rotate+store, history, raw, finalize, window store
+LAYER = "model.layers.0.self_attn.attn"
+
+
+def plugin_for(st, device, workdir):
+    """What a vLLM worker holds for one OSCAR layer: the attention impl (rotations loaded
+    from .pt files after "weight loading"), the metadata builder, and the step's common
+    attention metadata (vLLM's per-step device tensors)."""
+    from types import SimpleNamespace
+
+    from oscar_new_b200.backend import OscarAttentionImpl
+    from oscar_new_b200.metadata import OscarMetadataBuilder
+
+    nr, h = st["requests"], st["kv_heads"]
+    for name, rot in (("K", st["rk"]), ("V", st["rv"])):
+        path = os.path.join(workdir, f"{name.lower()}_rotation.pt")
+        torch.save({"layers": {0: {"rotation": rot.float().cpu()}}}, path)
+        os.environ[f"VLLM_OSCAR_{name}_ROTATION_PATH"] = path
+    os.environ["VLLM_OSCAR_SINK_TOKENS"] = str(SINK)
+    os.environ["VLLM_OSCAR_RECENT_TOKENS"] = str(RECENT)
+    vc = SimpleNamespace(
+        cache_config=SimpleNamespace(enable_prefix_caching=False, cache_dtype="auto"),
+        model_config=SimpleNamespace(dtype=torch.bfloat16, hf_text_config=SimpleNamespace(head_dim=D),
+                                     max_model_len=SEQ),
+        kv_transfer_config=None,
+        parallel_config=SimpleNamespace(decode_context_parallel_size=1, prefill_context_parallel_size=1,
+                                        enable_dbo=False),
+        speculative_config=None,
+        scheduler_config=SimpleNamespace(max_num_seqs=nr, max_num_batched_tokens=nr),
+        compilation_config=SimpleNamespace(static_forward_context={}),
+    )
+    impl = OscarAttentionImpl(h * G, D, 1.0 / math.sqrt(D), num_kv_heads=h, vllm_config=vc)
+    impl.initialize_layer(SimpleNamespace(layer_name=LAYER))
+    builder = OscarMetadataBuilder(SimpleNamespace(block_size=BP, num_kv_heads=h), [LAYER], vc, device)
+    if impl.cfg.sink_tokens != SINK or impl.cfg.recent_tokens != RECENT:
+        raise RuntimeError("plugin configuration differs from the workload")
+    m = st["meta"]
+    cm = SimpleNamespace(query_start_loc=m.query_start_loc[: nr + 1].clone(), seq_lens=m.seq_lens[:nr].clone(),
+                         block_table_tensor=m.block_tables[:nr].clone(), slot_mapping=m.slot_mapping[:nr].clone(),
+                         num_reqs=nr, num_actual_tokens=nr, max_query_len=1, max_seq_len=SEQ, causal=True)
+    return impl, builder, cm
+
+
+def count_launches(fn, device):
+    """Kernels of this library (namespace oscar) that one call of `fn` launches, from
+    the CUDA profiler; None if the profiler is unavailable (e.g. under ncu)."""
+    try:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize(device)
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        return sum(1 for nm in names if "oscar::" in nm)
+    except Exception:  # noqa: BLE001 - a profiler clash must not end the bench
+        return None
 
 
 class ClockSampler:
@@ -216,17 +276,26 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside), "window": where}
 
 
-def traffic_per_launch():
-    """dram bytes per history-kernel launch from the committed ncu summary (scaled)."""
+def traffic_per_launch(requests):
+    """DRAM bytes per history-kernel launch: the committed ncu capture (a smaller batch,
+    one launch), scaled to `requests` x the captured kv heads by the units processed."""
     p = ROOT / "profiles" / "history_attention_traffic.json"
     if not p.exists():
-        return None
+        return None, None
     d = json.loads(p.read_text())
-    return d["dram_bytes_per_launch_scaled_to_bench"]
+    captured = d["dram_bytes_read_captured"] + d["dram_bytes_write_captured"]
+    n = d["requests_captured"]
+    return captured * requests / n, (f"not measured in this run: ncu capture of {n} requests x 4 KV heads "
+                                     f"({captured} B), scaled by {requests}/{n} ({p.name})")
+
+
+TARGET_REGION_S = 3.0  # each timed leg runs about this long, whatever --steps is
 
 
 def run_gpu(args):
     from oscar_new_b200 import _lib, kernels
+    from oscar_new_b200.config import decode_split_cap
+    from oscar_new_b200.partition import head_split, shard_of
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -241,10 +310,17 @@ def run_gpu(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     _lib.lib()
-    st = build_state(device, seed=1234 + rank)
-    sizes = workload_sizes()
-    out = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=device)
-    scratch = kernels.DecodeScratch(B, H * G, SPLITS, device)
+    # One global batch of B * world config-3 requests, split by KV head (tensor parallel,
+    # as the model shards its heads) and then by request: every rank gets B * tp requests
+    # x H / tp KV heads, the per-GPU work of N = 1.
+    tp = head_split(H, world)
+    shard = shard_of(rank, [SEQ] * (B * world), H, world)
+    st = build_state(device, seed=1234 + rank, requests=len(shard.requests), kv_heads=shard.kv_heads)
+    nr, h = st["requests"], st["kv_heads"]
+    sizes = workload_sizes(nr, h)
+    workdir = tempfile.mkdtemp(prefix="oscar_bench_")
+    impl, builder, cm = plugin_for(st, device, workdir)
+    stream = torch.cuda.current_stream(device)
 
     def barrier():
         if dist is not None:
@@ -258,114 +334,138 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident step (value) ----
-    for _ in range(args.warmup):
-        layer_step(st, out, scratch)
-    barrier()
-    stream = torch.cuda.current_stream(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device) as clocks:
-        t0 = time.time()
+    def timed(fn, steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
         e0.record(stream)
-        for _ in range(args.steps):
-            layer_step(st, out, scratch)
+        for _ in range(steps):
+            fn()
         e1.record(stream)
         barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    out = torch.empty((nr, h * G * D), dtype=torch.bfloat16, device=device)
+    q2, k2, v2 = (st[x].view(nr, -1) for x in ("q", "k", "v"))
+
+    def forward(q, k, v, o, meta):
+        impl.forward(None, q, k, v, st["cache"], meta, o)
+
+    # ---- inner repeats: a step is one metadata build + R layer forwards, R chosen from
+    # the warm-up so that every timed leg runs about TARGET_REGION_S seconds ----
+    meta = builder.build(0, cm)
+    for _ in range(args.warmup):
+        forward(q2, k2, v2, out, meta)
+    layer_ms = timed(lambda: forward(q2, k2, v2, out, meta), max(args.warmup, 3))
+    repeats = max(1, math.ceil(TARGET_REGION_S * 1e3 / (args.steps * layer_ms)))
+    repeats = int(max_over_ranks(repeats))
+
+    def step():
+        m = builder.build(0, cm)
+        for _ in range(repeats):
+            forward(q2, k2, v2, out, m)
+
+    launches = count_launches(step, device)
+    for _ in range(args.warmup):
+        step()
+    with ClockSampler(device) as clocks:
+        t0 = time.time()
+        step_ms = timed(step, args.steps)
         clocks.mark(t0, time.time())
-    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     if not bool(torch.isfinite(out.float()).all()):
         raise RuntimeError("non-finite attention output")
 
     # ---- dominant kernel alone: history split-KV attention, CUDA events on its stream ----
     m = st["meta"]
+    kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
+                          st["cfg"].queries_per_tile)
     qrot = kernels.rotate(st["q"], st["rk"])
+
+    def history():
+        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
+                                   1.0 / math.sqrt(D), SPLITS, False)
+
     for _ in range(3):
-        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
-                                   1.0 / math.sqrt(D), SPLITS, False)
-    barrier()
-    reps = max(5, args.steps)
-    e0.record(stream)
-    for _ in range(reps):
-        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"],
-                                   1.0 / math.sqrt(D), SPLITS, False)
-    e1.record(stream)
-    barrier()
-    kern_ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+        history()
+    kern_ms = timed(history, max(5, math.ceil(TARGET_REGION_S * 1e3 / max(layer_ms, 1e-3))))
 
-    # ---- end to end through the public API with host buffers ----
-    pin = {name: st[name].cpu().pin_memory() for name in ("q", "k", "v")}
-    meta_host = {name: getattr(m, name).cpu().pin_memory() for name in ("query_start_loc", "seq_lens", "slot_mapping")}
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    h2d_bytes = sum(t.numel() * t.element_size() for t in list(pin.values()) + list(meta_host.values()))
-    d2h = out_host.numel() * out_host.element_size()
-
-    # Serving-style pipeline: two sets of device inputs / outputs; a copy stream moves
-    # step i+1's inputs in (once step i-1, the previous user of that set, has finished)
-    # and step i's output out while step i computes.  Every step still copies its own
-    # inputs from pinned host memory and reads its own result back inside the timed region.
-    import copy as _copy
-
-    sets = [(st, m, out)]
-    st_b = dict(st)
-    for name in pin:
-        st_b[name] = torch.empty_like(st[name])
-    m_b = _copy.copy(m)
-    for name in meta_host:
-        setattr(m_b, name, torch.empty_like(getattr(m, name)))
-    st_b["meta"] = m_b
-    sets.append((st_b, m_b, torch.empty_like(out)))
-    outs_host = [out_host, torch.empty_like(out_host).pin_memory()]
+    # ---- end to end through the plugin with host buffers ----
+    # Per step: vLLM's per-step metadata (query starts, sequence lengths, slot mapping)
+    # goes host -> device and the builder stages it; per layer forward: that layer's
+    # Q/K/V go host -> device and its output device -> host.  Two device input / output
+    # sets: a copy stream moves call c+1's inputs in while call c computes, another
+    # reads call c's output back.  The block table stays device-resident, as in the
+    # runner (it changes only when a request gains a page).
+    pin = {x: st[x].view(nr, -1).cpu().pin_memory() for x in ("q", "k", "v")}
+    meta_pin = {x: getattr(cm, x).cpu().pin_memory() for x in ("query_start_loc", "seq_lens", "slot_mapping")}
+    dev_in = [{x: torch.empty_like(t, device=device) for x, t in pin.items()} for _ in range(2)]
+    dev_cm = []
+    for _ in range(2):
+        c2 = type(cm)(**vars(cm))
+        for x, t in meta_pin.items():
+            setattr(c2, x, torch.empty_like(t, device=device))
+        dev_cm.append(c2)
+    dev_out = [torch.empty_like(out) for _ in range(2)]
+    host_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
     up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
     h2d_done = [torch.cuda.Event() for _ in range(2)]
     d2h_done = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
+    layer_h2d = sum(t.numel() * t.element_size() for t in pin.values())
+    step_h2d = sum(t.numel() * t.element_size() for t in meta_pin.values())
+    layer_d2h = host_out[0].numel() * host_out[0].element_size()
 
-    def h2d(b):
-        s_b, m_b2, _ = sets[b]
+    def upload(b, with_meta):
         with torch.cuda.stream(up):
-            for name, t in pin.items():
-                s_b[name].copy_(t, non_blocking=True)
-            for name, t in meta_host.items():
-                getattr(m_b2, name).copy_(t, non_blocking=True)
+            for x, t in pin.items():
+                dev_in[b][x].copy_(t, non_blocking=True)
+            if with_meta:
+                for x, t in meta_pin.items():
+                    getattr(dev_cm[b], x).copy_(t, non_blocking=True)
             h2d_done[b].record(up)
 
     def e2e_run(steps):
+        calls = steps * repeats
         up.wait_stream(stream)
         down.wait_stream(stream)
-        h2d(0)
-        for i in range(steps):
-            b = i & 1
-            s_b, _, o_b = sets[b]
+        upload(0, True)
+        meta_now = None
+        for c in range(calls):
+            b = c & 1
             stream.wait_event(h2d_done[b])
-            if i >= 2:
-                stream.wait_event(d2h_done[b])  # step i-2's output has been read back
-            layer_step(s_b, o_b, scratch)
+            if c >= 2:
+                stream.wait_event(d2h_done[b])  # call c-2's output has been read back
+            if c % repeats == 0:
+                meta_now = builder.build(0, dev_cm[b])
+            forward(dev_in[b]["q"], dev_in[b]["k"], dev_in[b]["v"], dev_out[b], meta_now)
             done[b].record(stream)
-            if i + 1 < steps:
-                if i >= 1:
-                    up.wait_event(done[1 - b])  # step i-1, the other set's user, is done
-                h2d(1 - b)
+            if c + 1 < calls:
+                if c >= 1:
+                    up.wait_event(done[1 - b])  # call c-1, the other set's user, is done
+                upload(1 - b, (c + 1) % repeats == 0)
             with torch.cuda.stream(down):
                 down.wait_event(done[b])
-                outs_host[b].copy_(o_b, non_blocking=True)
+                host_out[b].copy_(dev_out[b], non_blocking=True)
                 d2h_done[b].record(down)
         stream.wait_stream(up)
         stream.wait_stream(down)
 
-    e2e_run(args.warmup)
-    barrier()
-    e0.record(stream)
-    e2e_run(args.steps)
-    e1.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_run(max(1, args.warmup // repeats + 1))
+    e2e_ms = timed(lambda: e2e_run(args.steps), 1) / args.steps
+    torch.cuda.synchronize(device)
+    last = host_out[(args.steps * repeats - 1) & 1].float()
+    ref_out = out.float().cpu()
+    e2e_rel = float((last - ref_out).norm() / ref_out.norm().clamp_min(1e-30))
+    if not e2e_rel < 1e-3:
+        raise RuntimeError(f"end-to-end output differs from the device-resident step (rel {e2e_rel})")
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = sizes["history_bytes"] / (kern_ms * 1e-3) / 1e9
+        traffic, traffic_note = traffic_per_launch(nr * h // H)
+        kv_per_step = world * sizes["kv_tokens"] * repeats
         line = {
             "metric": METRIC,
-            "value": world * sizes["kv_tokens"] / (step_ms * 1e-3),
+            "value": kv_per_step / (step_ms * 1e-3),
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
@@ -378,11 +478,19 @@ def run_gpu(args):
             "data": "synthetic (seeded N(0,1) bf16, K channels 0-7 x20, random-permutation pages)",
             "config": {
                 **decode_config(),
+                "global_batch": B * world,
+                "partition": f"KV heads tensor-parallel x{tp}, requests x{world // tp} (partition.py); "
+                             f"{nr} requests x {h} KV heads per GPU, no data-path collective",
+                "inner_repeats": repeats,
+                "step": f"one metadata build + {repeats} layer forwards (OscarMetadataBuilder.build, "
+                        f"OscarAttentionImpl.forward)",
+                "kv_splits": f"balanced per request, at most "
+                             f"{decode_split_cap(nr, h, 1, nr, h * G)} (forward's cap); roofline leg {SPLITS}",
                 "l2": "inputs larger than L2 (packed history 1.14 GB per GPU)",
-                "us_per_layer": step_ms * 1e3,
-                "hbm_gbs_algorithmic": sizes["algorithmic_bytes"] / (step_ms * 1e-3) / 1e9,
-                "frac_of_8tbs_packed_history": sizes["history_bytes"] / (step_ms * 1e-3) / 8e12,
-                "parallelism": f"weak x{world}, shard = requests x KV heads, no data-path collective",
+                "us_per_layer": step_ms * 1e3 / repeats,
+                "hbm_gbs_algorithmic": sizes["algorithmic_bytes"] * repeats / (step_ms * 1e-3) / 1e9,
+                "frac_of_8tbs_packed_history": sizes["history_bytes"] * repeats / (step_ms * 1e-3) / 8e12,
+                "parallelism": f"weak x{world}",
             },
             "roofline": {
                 "kernel": "history_attention_kernel",
@@ -394,24 +502,27 @@ def run_gpu(args):
                 "frac": achieved / peak,
                 "us_per_launch": kern_ms * 1e3,
                 "algorithmic_bytes_per_launch": sizes["history_bytes"],
-                "traffic": traffic_per_launch(),
+                "traffic": traffic,
+                "traffic_source": traffic_note,
             },
             "e2e": {
-                "value": world * sizes["kv_tokens"] / (e2e_ms * 1e-3),
+                "value": kv_per_step / (e2e_ms * 1e-3),
                 "unit": UNIT,
-                "h2d_bytes_per_step": h2d_bytes,
-                "d2h_bytes_per_step": d2h,
+                "h2d_bytes_per_step": step_h2d + repeats * layer_h2d,
+                "d2h_bytes_per_step": repeats * layer_d2h,
                 "ms_per_step": e2e_ms,
-                "pipelining": "step i+1 host->device inputs (one copy stream) and step i-1 device->host "
-                              "output (another) overlap step i (two device input/output sets)",
+                "path": "OscarMetadataBuilder.build + OscarAttentionImpl.forward with pinned host inputs/outputs",
+                "rel_err_vs_device_step": e2e_rel,
+                "pipelining": "call c+1's host->device inputs (one copy stream) and call c's device->host output "
+                              "(another) overlap call c (two device input/output sets)",
             },
-            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "gpu_launches": None if launches is None else launches * args.steps,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(st, budget_s=args.cpu_budget)
+            scratch = kernels.DecodeScratch(nr, h * G, SPLITS, device)
+            line["cpu_baseline"] = cpu_baseline(st, scratch, budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
-    del scratch
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -443,7 +554,7 @@ def oracle_decode_sample(history, window, meta, layout, qrot, q, k, v, rv, reque
     return torch.cat(outs)
 
 
-def cpu_baseline(st, budget_s=20.0):
+def cpu_baseline(st, scratch, budget_s=20.0):
     torch.set_num_threads(os.cpu_count() or 1)
     from oscar_new_b200 import kernels
 
@@ -466,7 +577,6 @@ def cpu_baseline(st, budget_s=20.0):
     if out is not None:
         # spot parity of the last sampled request against the GPU output
         gpu = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=st["q"].device)
-        scratch = kernels.DecodeScratch(B, H * G, SPLITS, st["q"].device)
         layer_step(st, gpu, scratch)
         g = gpu.view(B, H * G, D)[done - 1].float().cpu()
         check = float((g - out[0]).norm() / out[0].norm())

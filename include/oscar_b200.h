@@ -87,6 +87,17 @@ int oscar_version(void);
  * an error status, not a hang, and that the context stays usable. */
 int oscar_selftest_bounded_wait(int32_t *status, void *stream);
 
+/* Which history kernel the latest successful history launch of this process used
+ * (a host-side record made at launch time; no device access): 0 none yet,
+ * OSCAR_HISTORY_ATTENTION_KERNEL (mma.sync, decode and general rows),
+ * OSCAR_HISTORY_MTP_KERNEL (mma.sync, MTP verify rows) or OSCAR_HISTORY_F8_KERNEL
+ * (tcgen05 e4m3, opt-in with OSCAR_HISTORY_F8=1).  Diagnostics for tests and
+ * deployments that need to know the dispatch; no reference counterpart. */
+#define OSCAR_HISTORY_ATTENTION_KERNEL 1
+#define OSCAR_HISTORY_MTP_KERNEL 2
+#define OSCAR_HISTORY_F8_KERNEL 3
+int oscar_last_history_kernel(void);
+
 /* Test hook for the timeout path of the decode history kernels (no counterpart in the
  * reference): from the next launch on, CTA (0, 0, 0) of every history launch (the default
  * mma.sync kernels and the opt-in tcgen05 kernel) never issues the copy of its chunk / tile
@@ -145,8 +156,9 @@ int oscar_step_arena_layout(int32_t max_reqs, int32_t columns, int32_t task_capa
  * num_tokens}; query starts [0, num_reqs], sequence lengths [0, num_reqs); block-table
  * columns [0, copy_columns) of rows [0, num_reqs) (source rows `table_stride` apart);
  * slot_out[0, num_tokens) = slots; and the compact task table built from the source
- * query starts.  num_reqs = num_tokens = 0 is the dummy / capture step: counts and task
- * count become 0 and nothing else is touched.  Replaces the reference builder's copies,
+ * query starts.  qstarts may be null only when num_reqs = 0: with num_tokens = 0 too
+ * that is the dummy / capture step, whose counts and task count become 0 and nothing
+ * else is touched.  Replaces the reference builder's copies,
  * fills and prepare_tasks call (metadata.py:108-145, kernels.py:222-287). */
 int oscar_stage_step_metadata(const int32_t *qstarts, const int32_t *seq_lens, const int32_t *table,
                               int64_t table_stride, const int64_t *slots, int32_t num_reqs,

@@ -1012,6 +1012,9 @@ static bool history_f8_enabled() {
   return v != nullptr && v[0] == '1';
 }
 
+// The history kernel of the latest successful history launch (oscar_last_history_kernel).
+static std::atomic<int32_t> g_last_history{0};
+
 // Test hook state (oscar_test_set_wait_fault), read at every history launch.
 static std::atomic<int32_t> g_withhold{-1};
 static std::atomic<uint32_t> g_wait_probes{kWaitLimit};
@@ -1021,10 +1024,12 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, 
   P.wait_probes = g_wait_probes.load();
   if (history_f8_enabled()) {
     const int rc = history_f8_launch(P, num_tasks, sm_count(), stream, priority);
+    if (rc == OSCAR_OK) g_last_history.store(OSCAR_HISTORY_F8_KERNEL);
     if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
   }
   if (history_mtp_enabled()) {
     const int rc = history_mtp_launch(P, num_tasks, stream, priority);
+    if (rc == OSCAR_OK) g_last_history.store(OSCAR_HISTORY_MTP_KERNEL);
     if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
   }
   const oscar_geometry &g = P.geo;
@@ -1052,9 +1057,11 @@ static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, 
   if (smem < 128 + xch) smem = 128 + xch;
   if (smem > 227 * 1024) return OSCAR_ERR_UNSUPPORTED;
   dim3 grid(num_tasks, P.splits, g.kv_heads / hpc);
-  if (narrow) return launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream, priority);
-  if (mid) return launch_history<kMidWarps, NM, 4, 1>(P, grid, smem, stream, priority);
-  return launch_history<kMaxConsumerWarps, NM, 4, 1>(P, grid, smem, stream, priority);
+  const int rc = narrow ? launch_history<kNarrowWarps, NM, 3, kNarrowCtasPerSm>(P, grid, smem, stream, priority)
+                 : mid    ? launch_history<kMidWarps, NM, 4, 1>(P, grid, smem, stream, priority)
+                          : launch_history<kMaxConsumerWarps, NM, 4, 1>(P, grid, smem, stream, priority);
+  if (rc == OSCAR_OK) g_last_history.store(OSCAR_HISTORY_ATTENTION_KERNEL);
+  return rc;
 }
 
 // Side stream of the decode step's BF16 raw path (one per device, created on first use):
@@ -1321,3 +1328,5 @@ extern "C" int oscar_test_set_wait_fault(int32_t withhold, uint32_t wait_probes)
   g_wait_probes.store(wait_probes == 0 ? kWaitLimit : wait_probes);
   return OSCAR_OK;
 }
+
+extern "C" int oscar_last_history_kernel(void) { return g_last_history.load(); }

@@ -10,9 +10,10 @@
 // the task table (built from the source query starts directly), the other blocks copy
 // the reachable block-table columns and the slot mapping.
 //
-// A dummy step (graph capture, warm-up) stages zero requests and zero tokens: the
-// counts and the task count become 0, which masks every cache access of the recorded
-// kernels, and nothing else is read or written.
+// A dummy step (graph capture, warm-up) stages zero requests and zero tokens with no
+// sources: the counts and the task count become 0, which masks every cache access of
+// the recorded kernels, and nothing else is read or written.  A real step of zero
+// requests still copies its one query start.
 #include <algorithm>
 
 #include "common.cuh"
@@ -58,11 +59,9 @@ __global__ void __launch_bounds__(1024) stage_step_kernel(StageArgs a) {
       a.arena[0] = a.nr;
       a.arena[1] = a.nt;
     }
-    for (int i = threadIdx.x; i < a.nr; i += blockDim.x) {
-      q[i] = a.qstarts[i];
-      s[i] = a.seq_lens[i];
-    }
-    if (threadIdx.x == 0 && a.nr > 0) q[a.nr] = a.qstarts[a.nr];
+    if (a.qstarts)
+      for (int i = threadIdx.x; i <= a.nr; i += blockDim.x) q[i] = a.qstarts[i];
+    for (int i = threadIdx.x; i < a.nr; i += blockDim.x) s[i] = a.seq_lens[i];
     build_task_table(a.qstarts, a.nr, a.nt, a.arena + a.L.tasks, a.arena + 2, a.capacity, a.query_tile);
     return;
   }

@@ -211,25 +211,27 @@ def step_arena_layout(max_reqs: int, columns: int, task_capacity: int) -> dict:
 def stage_step_metadata(arena, slot_out, max_reqs, columns, task_capacity, query_tile, num_reqs=0, num_tokens=0,
                         qstarts=None, seq_lens=None, table=None, slots=None, copy_columns=0):
     """Stage one step's metadata into the fixed arena in one launch (counts, query starts,
-    sequence lengths, reachable block-table columns, slot mapping, task table).  Zero
-    requests and tokens stage a dummy step: counts and task count 0, nothing else."""
+    sequence lengths, reachable block-table columns, slot mapping, task table).  No
+    sources and zero requests / tokens stage a dummy step: counts and task count 0,
+    nothing else."""
     _require_cuda(arena, slot_out, qstarts, seq_lens, table, slots)
     if arena.dtype != torch.int32 or slot_out.dtype != torch.int64:
         raise ValueError("the arena is int32 and the slot buffer int64")
-    if num_reqs:
-        qstarts, seq_lens = qstarts.to(torch.int32), seq_lens.to(torch.int32)
-        if table is not None and copy_columns:
-            if table.dtype != torch.int32 or table.stride(1) != 1:
-                table = table.to(torch.int32).contiguous()
-        else:
-            table, copy_columns = None, 0
-    if num_tokens:
-        slots = slots.to(torch.int64)
-    _lib.call("oscar_stage_step_metadata", _ptr(qstarts if num_reqs else None),
-              _ptr(seq_lens if num_reqs else None), _ptr(table if num_reqs else None),
-              table.stride(0) if num_reqs and table is not None else 0, _ptr(slots if num_tokens else None),
-              num_reqs, num_tokens, copy_columns if num_reqs else 0, query_tile, arena.data_ptr(), max_reqs, columns,
-              task_capacity, slot_out.data_ptr(), slot_out.shape[0], _stream(arena))
+    if qstarts is not None:
+        qstarts = qstarts.to(torch.int32)
+    if not num_reqs:
+        seq_lens = table = None
+    if seq_lens is not None:
+        seq_lens = seq_lens.to(torch.int32)
+    if table is None or not copy_columns:
+        table, copy_columns = None, 0
+    elif table.dtype != torch.int32 or table.stride(1) != 1:
+        table = table.to(torch.int32).contiguous()
+    slots = slots.to(torch.int64) if num_tokens else None
+    _lib.call("oscar_stage_step_metadata", _ptr(qstarts), _ptr(seq_lens), _ptr(table),
+              0 if table is None else table.stride(0), _ptr(slots), num_reqs, num_tokens, copy_columns, query_tile,
+              arena.data_ptr(), max_reqs, columns, task_capacity, slot_out.data_ptr(), slot_out.shape[0],
+              _stream(arena))
 
 
 def _meta_common(meta, layout, hq):

@@ -45,15 +45,18 @@ class Scenario:
     """A batch of requests with full K/V sequences, a paged cache and step metadata."""
 
     def __init__(self, seq_lens, query_lens, hq, h, cfg, block_tokens=768, seed=0, device="cuda", fill="oracle",
-                 rk=None, rv=None, max_reqs=None):
+                 rk=None, rv=None, max_reqs=None, data=None):
         self.cfg = cfg
         self.layout = CacheLayout(block_tokens, kv_heads=h, config=cfg)
         self.plan = plan_pages(seq_lens, query_lens, block_tokens, seed=seed, max_reqs=max_reqs)
         gen = torch.Generator().manual_seed(1000 + seed)
         self.hq, self.h = hq, h
-        self.ks = [oo_outlier(gen, s, h) for s in seq_lens]
-        self.vs = [torch.randn(s, h, 256, generator=gen).bfloat16() for s in seq_lens]
-        self.qs = [torch.randn(q, hq, 256, generator=gen).bfloat16() for q in query_lens]
+        if data is None:
+            self.ks = [oo_outlier(gen, s, h) for s in seq_lens]
+            self.vs = [torch.randn(s, h, 256, generator=gen).bfloat16() for s in seq_lens]
+            self.qs = [torch.randn(q, hq, 256, generator=gen).bfloat16() for q in query_lens]
+        else:  # given per-request K/V [s, h, 256] and Q [q, hq, 256] (e.g. one rank's shard)
+            self.ks, self.vs, self.qs = (list(x) for x in data)
         self.prefixes = [s - q for s, q in zip(seq_lens, query_lens)]
         from oscar_new_b200.synthetic import rotation
 
@@ -104,3 +107,45 @@ def oo_outlier(gen, n, h):
     x = torch.randn(n, h, 256, generator=gen)
     x[..., :8] *= 20
     return x.bfloat16()
+
+
+def shard_scenario(sc, shard, seed=0):
+    """The Scenario one rank of a KV head x request partition holds: its requests (in
+    shard order) and its KV heads with their query heads, same rotations and config."""
+    g = sc.hq // sc.h
+    hb, he = shard.head_begin, shard.head_end
+    reqs = list(shard.requests)
+    data = ([sc.ks[r][:, hb:he].contiguous() for r in reqs], [sc.vs[r][:, hb:he].contiguous() for r in reqs],
+            [sc.qs[r][:, hb * g:he * g].contiguous() for r in reqs])
+    return Scenario([sc.plan.seq_lens[r] for r in reqs], [sc.plan.query_lens[r] for r in reqs], hq=(he - hb) * g,
+                    h=he - hb, cfg=sc.cfg, block_tokens=sc.layout.physical_block_tokens, seed=seed,
+                    device=sc.device, rk=sc.rk, rv=sc.rv, data=data)
+
+
+def fill_prefixes_on_device(plan, layout, history, window, rk, rv, seed, chunk=16384):
+    """Write every request's prefix (seeded bf16 K/V, K channels 0-7 x20, generated on
+    the device chunk by chunk) with the product store kernels: INT2 history through
+    rotate_store, the BF16 sink / ring window through store_windows.  For contexts too
+    long to pack on the host; the store kernels' bytes equal the oracle's (store parity
+    tests), and the oracle then reads the cache these calls wrote."""
+    device = history.device
+    gen = torch.Generator(device=device).manual_seed(seed)
+    h = layout.kv_heads
+    for req, (sq, ql) in enumerate(zip(plan.seq_lens, plan.query_lens)):
+        prefix = sq - ql
+        for s0 in range(0, prefix, chunk):
+            n = min(chunk, prefix - s0)
+            k = torch.randn(n, h, 256, device=device, generator=gen)
+            k[..., :8] *= 20
+            k = k.bfloat16()
+            v = torch.randn(n, h, 256, device=device, generator=gen).bfloat16()
+            slots = plan.slots_of(req, range(s0, s0 + n)).to(device)
+            counts = torch.tensor([1, n], dtype=torch.int32, device=device)
+            kernels.rotate_store(k, v, rk, rv, history, slots, counts, layout)
+            m1 = plan.meta(device)
+            m1.query_start_loc = torch.tensor([0, n], dtype=torch.int32, device=device)
+            m1.seq_lens = torch.tensor([s0 + n], dtype=torch.int32, device=device)
+            m1.block_tables = plan.block_tables[req: req + 1].to(device).contiguous()
+            m1.counts = counts
+            m1.max_num_reqs = 1
+            kernels.store_windows(k, v, window, m1, layout)
