@@ -11,6 +11,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -506,11 +507,35 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
 
 using namespace oscar;
 
+namespace oscar {
+int gram_tc_launch(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int32_t groups,
+                   const float *weights, float *cov, int32_t *status, int sm_count, cudaStream_t stream);
+}
+
+// The tcgen05 Gram (gram_tc.cu) is the default; OSCAR_GRAM_MMA=1 (read at every call)
+// selects the mma.sync gram_kernel, which also serves layouts a tensor map cannot take.
+static bool gram_mma_forced() {
+  const char *v = getenv("OSCAR_GRAM_MMA");
+  return v != nullptr && v[0] == '1';
+}
+
+static int device_sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return sms;
+}
+
 static int launch_gram(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int32_t groups,
                        const float *weights, float *cov, void *stream) {
   if (n < 0 || h <= 0 || groups <= 0 || h % groups || !cov) return OSCAR_ERR_INVALID;
   if (n == 0) return OSCAR_OK;
   if (!x || (reinterpret_cast<uintptr_t>(x) & 15) || xs0 % 8 || xs1 % 8) return OSCAR_ERR_INVALID;
+  if (!gram_mma_forced()) {
+    const int rc = gram_tc_launch(x, n, h, xs0, xs1, groups, weights, cov, nullptr, device_sm_count(),
+                                  (cudaStream_t)stream);
+    if (rc != OSCAR_ERR_UNSUPPORTED) return rc;
+  }
   const int hpg = h / groups;
   const int64_t rows = n * hpg;
   // chunks sized so that the launch covers about two waves of 148 SMs

@@ -158,7 +158,6 @@ OSCAR_DEVINL void f8_drain(uint64_t *bar, uint32_t parity, uint32_t probes) {
 }
 
 OSCAR_DEVINL void named_sync128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-OSCAR_DEVINL void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 OSCAR_DEVINL int blocks_of(const TaskInfo &ti) {
   const int length = ti.recent_begin - ti.sink_len;

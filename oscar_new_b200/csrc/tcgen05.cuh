@@ -29,6 +29,9 @@ OSCAR_DEVINL void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y
       : "memory");
 }
 
+// Generic-proxy shared-memory writes become visible to the async proxy (TMA, tcgen05.mma).
+OSCAR_DEVINL void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 OSCAR_DEVINL void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 OSCAR_DEVINL void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 

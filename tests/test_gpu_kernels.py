@@ -616,6 +616,39 @@ def test_streamed_covariances_against_fp64(cuda_lib):
     torch.testing.assert_close(got, expect_v, atol=2e-4, rtol=2e-4)
 
 
+@pytest.mark.parametrize("weighted", [False, True])
+def test_gram_tcgen05_matches_fp64_and_the_mma_sync_gram(cuda_lib, monkeypatch, weighted):
+    """The tcgen05 Gram (default) on grouped rows: 24 query heads in 4 groups of 6 (a
+    64-row block holds 60 rows), or 4 KV heads one per group with per-row weights;
+    1003 tokens (not a multiple of a block), a strided view, outlier channels.  Against
+    fp64 and against the mma.sync Gram (OSCAR_GRAM_MMA=1)."""
+    torch.manual_seed(57 + weighted)
+    n, h, groups = (1003, 4, 4) if weighted else (1003, 24, 4)
+    x = torch.randn(n, 2 * h, 256)
+    x[..., :8] *= 20
+    x = x.bfloat16()[:, ::2]
+    w = torch.rand(n * h) * 3 if weighted else None
+    hpg = h // groups
+    xd = x.double().view(n, groups, hpg, 256)
+    wd = None if w is None else w.double().view(n, groups, hpg, 1)
+    expect = torch.einsum("ngpi,ngpj->gij", xd, xd if wd is None else xd * wd)
+
+    def run():
+        cov = torch.zeros((groups, 256, 256), device=DEV)
+        ck.accumulate_gram_grouped(x.to(DEV), cov, None if w is None else w.to(DEV))
+        return cov
+
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        got = run()
+        torch.cuda.synchronize()
+    assert any("gram_tc_kernel" in e.name for e in prof.events())
+    scale = float(expect.abs().max())
+    torch.testing.assert_close(got.cpu().double(), expect, rtol=1e-5, atol=2e-6 * scale)
+    monkeypatch.setenv("OSCAR_GRAM_MMA", "1")
+    ref = run()
+    torch.testing.assert_close(got, ref, rtol=1e-5, atol=2e-6 * scale)
+
+
 def test_sst_weights_match_fp64(cuda_lib):
     """w = max(k C k^T, 0) per row and the weight totals against fp64: per-head and
     shared covariances (outlier channels), 150 tokens (not a multiple of the 64-row
