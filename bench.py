@@ -1080,6 +1080,15 @@ def profile_only(what):
     st = build_state(device, seed=1234)
     m = st["meta"]
     out = torch.empty((B, H * G * D), dtype=torch.bfloat16, device=device)
+    if what == "forward":
+        # the timed decode step: one metadata build + one layer forward, four times
+        impl, builder, cm = plugin_for(st, device, tempfile.mkdtemp(prefix="oscar_prof_"))
+        q2, k2, v2 = (st[x].view(B, -1) for x in ("q", "k", "v"))
+        for _ in range(4):
+            impl.forward(None, q2, k2, v2, st["cache"], builder.build(0, cm), out)
+        torch.cuda.synchronize(device)
+        print("profile run done", B, "requests, build + forward")
+        return
     scratch = kernels.DecodeScratch(B, H * G, SPLITS, device)
     kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
                           st["cfg"].queries_per_tile)
@@ -1103,7 +1112,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
-    ap.add_argument("--profile-kernel", choices=["history", "step", "rotate-store", "mtp-verify", "calibration"],
+    ap.add_argument("--profile-kernel", choices=["history", "step", "forward", "rotate-store", "mtp-verify",
+                                                 "calibration"],
                     default=None,
                     help="build the state, run 4 launches of the kernel (or 4 layer steps) and exit")
     ap.add_argument("--workload", choices=["decode", "rotate-store", "mtp-verify", "calibration"], default="decode",
