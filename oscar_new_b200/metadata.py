@@ -145,6 +145,18 @@ def _first_prefill_starts(cm, num_reqs: int):
     return None
 
 
+def _page_tokens(kv_cache_spec, vllm_config) -> int:
+    """Tokens per physical cache page.  vLLM hands the builder a spec in the backend's
+    128-token kernel blocks when the engine's cache block (e.g. 768) is larger; the
+    kernel blocks of one engine block are consecutive in memory, so the engine block is
+    the page that holds a request's history and BF16 window."""
+    spec = kv_cache_spec.block_size
+    engine = getattr(getattr(vllm_config, "cache_config", None), "block_size", None)
+    if isinstance(engine, int) and engine > spec and engine % spec == 0:
+        return engine
+    return spec
+
+
 class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
     supports_update_block_table = False
     _cudagraph_support = AttentionCGSupport.UNIFORM_BATCH
@@ -160,7 +172,7 @@ class OscarMetadataBuilder(AttentionMetadataBuilder[OscarMetadata]):
             raise TypeError(f"OSCAR attention implementation replaced on layers {replaced}")
         spec = vllm_config.speculative_config
         cfg = OscarConfig.from_env(spec.num_speculative_tokens if spec else 0)
-        self.layout = CacheLayout(kv_cache_spec.block_size, kv_cache_spec.num_kv_heads, config=cfg)
+        self.layout = CacheLayout(_page_tokens(kv_cache_spec, vllm_config), kv_cache_spec.num_kv_heads, config=cfg)
         self.capacity = StepCapacity.for_engine(vllm_config, self.layout, cfg)
         self.buffers = StepBuffers(self.capacity, device)
         self.reorder_batch_threshold = cfg.speculative_tokens + 1
