@@ -238,27 +238,43 @@ class CalibrationWorkerExtension:
         return finish(self, output_dir, provenance, max_sweeps)
 
 
+# Native attention implementations vLLM may pick on a CUDA worker (FlashInfer on B200,
+# FlashAttention elsewhere); calibration observes whichever ones the engine loaded.
+NATIVE_IMPLS = (("vllm.v1.attention.backends.flash_attn", "FlashAttentionImpl"),
+                ("vllm.v1.attention.backends.flashinfer", "FlashInferImpl"))
+
+
 def install_hook(impl_cls=None):
-    """Wrap the native attention implementation's ``forward`` to observe Q/K/V."""
+    """Wrap the native attention implementations' ``forward`` to observe Q/K/V."""
     global _installed
     if _installed:
         return
-    if impl_cls is None:
-        module = sys.modules.get("vllm.v1.attention.backends.flash_attn")
-        impl_cls = getattr(module, "FlashAttentionImpl", None)
-        if impl_cls is None or getattr(getattr(module, "__spec__", None), "_initializing", False):
+    if impl_cls is not None:
+        classes = [impl_cls]
+    else:
+        classes = []
+        for module_name, name in NATIVE_IMPLS:
+            module = sys.modules.get(module_name)
+            if module is None or getattr(getattr(module, "__spec__", None), "_initializing", False):
+                continue
+            if getattr(module, name, None) is not None:
+                classes.append(getattr(module, name))
+        if not classes:
             raise RuntimeError("Native attention must be initialized before calibration begin RPC")
-    original = impl_cls.forward
+    for cls in classes:
+        original = cls.forward
 
-    @functools.wraps(original)
-    def forward(impl, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs):
-        result = original(impl, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs)
-        if _session is not None and _session.phase and attn_metadata is not None and key is not None \
-                and value is not None:
-            observe(impl, layer, query, key, value, attn_metadata.num_actual_tokens)
-        return result
+        def make(original):
+            @functools.wraps(original)
+            def forward(impl, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs):
+                result = original(impl, layer, query, key, value, kv_cache, attn_metadata, *args, **kwargs)
+                if _session is not None and _session.phase and attn_metadata is not None and key is not None \
+                        and value is not None:
+                    observe(impl, layer, query, key, value, attn_metadata.num_actual_tokens)
+                return result
+            return forward
 
-    impl_cls.forward = forward
+        cls.forward = make(original)
     _installed = True
 
 

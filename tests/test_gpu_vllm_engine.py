@@ -18,10 +18,16 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def run_engine(mode, oscar=1):
+def _env():
     env = dict(os.environ)
+    env["PYTHONPATH"] = str(ROOT) + os.pathsep + env.get("PYTHONPATH", "")
+    return env
+
+
+def run_engine(mode, oscar=1, *extra):
     out = subprocess.run([sys.executable, str(ROOT / "tests" / "vllm_engine_run.py"), "--mode", mode, "--oscar",
-                          str(oscar)], env=env, capture_output=True, text=True, timeout=900, cwd=str(ROOT))
+                          str(oscar), *extra], env=_env(), capture_output=True, text=True, timeout=900,
+                         cwd=str(ROOT))
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
     assert out.returncode == 0 and lines, out.stderr[-4000:]
     return json.loads(lines[-1])
@@ -46,3 +52,38 @@ def test_first_token_matches_the_native_backend(cuda_lib):
     assert native["impls"] and "Oscar" not in native["impls"][0]
     oscar = run_engine("eager", oscar=1)
     assert [t[0] for t in oscar["tokens"]] == [t[0] for t in native["tokens"]]
+
+
+def test_calibrate_on_the_engine_then_serve_with_the_published_rotations(cuda_lib, tmp_path):
+    """The calibration driver (reference calibrate.py on vLLM's CUDA worker): native
+    attention observed by the worker extension over 1024 synthetic tokens, both passes,
+    the device eigensolver, and k_rotation.pt / v_rotation.pt published for both layers;
+    then the engine serves through OSCAR with those rotations."""
+    import torch
+
+    from oscar_new_b200.rotations import get_rotation, load_checkpoint
+
+    model, out = tmp_path / "model", tmp_path / "rotations"
+    run = subprocess.run([sys.executable, str(ROOT / "tests" / "vllm_engine_run.py"), "--make-only",
+                          "--model-dir", str(model)], env=_env(), capture_output=True, text=True, timeout=600)
+    assert run.returncode == 0, run.stderr[-3000:]
+    run = subprocess.run([sys.executable, "-m", "oscar_new_b200.calibrate", "--model", str(model), "--output-dir",
+                          str(out), "--model-fingerprint", "tiny-qwen3", "--profile-fingerprint", "test",
+                          "--synthetic-prompts", "2", "--tokens", "1024", "--max-sweeps", "12", "--memory", "0.25"],
+                         env=_env(), capture_output=True, text=True, timeout=900, cwd=str(ROOT))
+    assert run.returncode == 0, run.stderr[-4000:]
+    for kind in ("k", "v"):
+        raw = torch.load(out / f"{kind}_rotation.pt", weights_only=False)
+        assert raw["calibration"]["model_fingerprint"] == "tiny-qwen3"
+        assert raw["calibration"]["prompt_tokens"] == 1024
+        assert sorted(raw["layers"]) == [0, 1]
+        for layer in (0, 1):
+            ev = raw["layers"][layer]["eigenvalues"]
+            assert bool((ev[1:] >= ev[:-1]).all()) and bool((ev > 0).all())
+        f = load_checkpoint(str(out / f"{kind}_rotation.pt"))
+        assert not f.problems
+        r = get_rotation(str(out / f"{kind}_rotation.pt"), "model.layers.1.self_attn.attn", "cpu").float()
+        assert float((r.T @ r - torch.eye(256)).abs().max()) < 0.015
+    r = run_engine("eager", 1, "--model-dir", str(model), "--rotations", str(out))
+    assert r["impls"] == ["oscar_new_b200.backend.OscarAttentionImpl"]
+    assert r["last_history_kernel"] in (1, 2, 3)

@@ -19,27 +19,46 @@ ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["eager", "graphs"], default="eager")
-    ap.add_argument("--oscar", type=int, default=1)
-    args = ap.parse_args()
-    os.environ["OSCAR_ENABLED"] = str(args.oscar)
-    os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
+def make_tiny_model(d: Path):
+    """Seeded random-weight Qwen3-architecture decoder: 2 layers, hidden 1024, 24 query /
+    4 KV heads of D = 256, vocabulary 2048 (written once per directory)."""
     import torch
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
-    d = Path(tempfile.mkdtemp(prefix="oscar_tiny_"))
+    if (d / "config.json").exists():
+        return
     cfg = Qwen3Config(vocab_size=2048, hidden_size=1024, intermediate_size=2048, num_hidden_layers=2,
                       num_attention_heads=24, num_key_value_heads=4, head_dim=256, max_position_embeddings=8192,
                       tie_word_embeddings=False)
     torch.manual_seed(0)
     Qwen3ForCausalLM(cfg).to(torch.bfloat16).save_pretrained(d)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["eager", "graphs"], default="eager")
+    ap.add_argument("--oscar", type=int, default=1)
+    ap.add_argument("--model-dir", default=None, help="reuse / create the tiny model here")
+    ap.add_argument("--make-only", action="store_true", help="write the tiny model and exit")
+    ap.add_argument("--rotations", default=None, help="directory with k_rotation.pt / v_rotation.pt")
+    args = ap.parse_args()
+    os.environ["OSCAR_ENABLED"] = str(args.oscar)
+    os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
+    import torch
+
+    d = Path(args.model_dir) if args.model_dir else Path(tempfile.mkdtemp(prefix="oscar_tiny_"))
+    d.mkdir(parents=True, exist_ok=True)
+    make_tiny_model(d)
+    if args.make_only:
+        return
     from oscar_new_b200.synthetic import rotation
 
     for name, seed in (("K", 1), ("V", 2)):
-        p = d / f"{name.lower()}_rotation.pt"
-        torch.save({"layers": {i: {"rotation": rotation(seed)} for i in range(2)}}, p)
+        if args.rotations:
+            p = Path(args.rotations) / f"{name.lower()}_rotation.pt"
+        else:
+            p = d / f"{name.lower()}_rotation.pt"
+            torch.save({"layers": {i: {"rotation": rotation(seed)} for i in range(2)}}, p)
         os.environ[f"VLLM_OSCAR_{name}_ROTATION_PATH"] = str(p)
     os.environ["VLLM_OSCAR_SINK_TOKENS"] = "4"
     os.environ["VLLM_OSCAR_RECENT_TOKENS"] = "128"
