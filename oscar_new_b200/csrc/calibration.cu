@@ -275,13 +275,13 @@ constexpr int kJThreads = 512;  // 16 warps: a round is latency-bound (remote ro
 constexpr int kJWarps = kJThreads / 32;
 
 struct JacobiSmem {
-  double a[kJRows][kDim];   // local rows of A at the start of a round
-  double nx[kJRows][kDim];  // local rows of A J (column-rotated), read by the partner rows' owners
-  double u[kJRows][kDim];
+  double a[kJRows][kDim];  // local rows of W = C V (columns rotated every round); epilogue scratch
+  double u[kJRows][kDim];  // local rows of V (the accumulated rotations)
   double cs[kDim / 2][2];
+  double part4[4][kDim / 2][3];           // per row group: a_pp, a_qq, a_pq of each pair
+  double all[2][kJCtas][kDim / 2][3];     // every CTA's sums, pushed here; double-buffered by round
   double diag[kDim];
-  double stat[2];
-  int flag[2];
+  double evpart[kDim];                    // this CTA's share of the Rayleigh quotients
 };
 
 // x mod (D-1) for x in (-(D-1), 2(D-1)): two conditional corrections, no division.
@@ -300,8 +300,32 @@ OSCAR_DEVINL void round_pair(int j, int r, int &p, int &q) {
   }
 }
 
-// The arithmetic is carried in fp64 (the reference uses fp32): same rotations, skip rule
-// and stopping rule, but eigenvalues accurate to the fp32 input.
+// Cyclic Jacobi with the reference's rotations (two-sided on A = V^T C V), carried out
+// on columns only: V starts as I and W = C V as C, and every round applies the 128
+// disjoint rotations of the reference's round-robin schedule to the columns of both.
+// The rotation of pair (p, q) needs a_pp = v_p . w_p, a_qq = v_q . w_q and
+// a_pq = v_p . w_q, the entries of the implicit A; its formula, skip rule and
+// convergence test (max|a_pq| / max|a_pp| of a sweep) are the reference's.  Column
+// updates are row-local, so a round needs only the cluster sums of the three dot
+// products (each CTA's sums over its 32 rows, read over distributed shared memory) and
+// ONE cluster barrier, where the row-rotating form exchanged partner rows with two.
+// The eigenvalues are the Rayleigh quotients v_p . w_p.  fp64 arithmetic (the
+// reference uses fp32).
+OSCAR_DEVINL double rsqrt_f64(double x) {
+  // fp32 seed, two Newton steps: about 46 bits, then the fp64 rounding
+  double y = (double)rsqrtf((float)x);
+  y = y * fma(-0.5 * x, y * y, 1.5);
+  y = y * fma(-0.5 * x, y * y, 1.5);
+  return y;
+}
+
+OSCAR_DEVINL double rcp_f64(double x) {
+  double y = (double)__frcp_rn((float)x);
+  y = y * fma(-x, y, 2.0);
+  y = y * fma(-x, y, 2.0);
+  return y;
+}
+
 __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__restrict__ cov, int32_t max_sweeps,
                                                              float tol, float *__restrict__ rot,
                                                              float *__restrict__ evals, float *__restrict__ info) {
@@ -322,126 +346,119 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
     S.a[r][c] = ((double)C[gr * kDim + c] + (double)C[c * kDim + gr]) * 0.5;
     S.u[r][c] = gr == c ? 1.0 : 0.0;
   }
-  cluster.sync();
+  __syncthreads();
   double residual = INFINITY;
   int sweeps_done = 0;
   bool finite = true;
+  int buf = 0;
   for (int sweep = 0; sweep < max_sweeps; ++sweep) {
-    // Two cluster barriers per round: the column-rotated rows go to a second buffer (nx),
-    // so the partner-row reads of step 3 never race with a write, and each CTA computes
-    // the rotation parameters of all pairs itself from the current rows.
+    double smax = 0.0, dmax = 0.0;  // largest |a_pq| and |a_pp| seen in this sweep
+    bool sfin = true;
     for (int r = 0; r < kDim - 1; ++r) {
-      // (1) rotation parameters of all pairs, from the (possibly remote) current rows
-      if (tid < kDim / 2) {
+      // (1) this CTA's a_pp, a_qq, a_pq of every pair of the round, over its 32 rows
+      {
+        const int j = tid & (kDim / 2 - 1), rg = tid >> 7;
         int p, q;
-        round_pair(tid, r, p, q);
-        const JacobiSmem *owner_p = cluster.map_shared_rank(&S, p / kJRows);
-        const JacobiSmem *owner_q = cluster.map_shared_rank(&S, q / kJRows);
-        const double app = owner_p->a[p % kJRows][p];
-        const double apq = owner_p->a[p % kJRows][q];
-        const double aqq = owner_q->a[q % kJRows][q];
-        const double delta = (aqq - app) * 0.5;
-        const double sgn = delta >= 0.0 ? 1.0 : -1.0;
-        double tang = sgn * apq / fmax(fabs(delta) + sqrt(delta * delta + apq * apq), 1e-30);
-        if (!(fabs(apq) > 1e-8 * (fabs(app) + fabs(aqq)) + 1e-20)) tang = 0.0;
-        const double cs = 1.0 / sqrt(1.0 + tang * tang);
-        S.cs[tid][0] = cs;
-        S.cs[tid][1] = tang * cs;
+        round_pair(j, r, p, q);
+        double app = 0.0, aqq = 0.0, apq = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int lr = rg * 8 + i;
+          const double vp = S.u[lr][p], vq = S.u[lr][q], wp = S.a[lr][p], wq = S.a[lr][q];
+          app = fma(vp, wp, app);
+          aqq = fma(vq, wq, aqq);
+          apq = fma(vp, wq, apq);
+        }
+        S.part4[rg][j][0] = app;
+        S.part4[rg][j][1] = aqq;
+        S.part4[rg][j][2] = apq;
       }
       __syncthreads();
-      // (2) column rotations of the local rows: nx = A J; U = U J in place
+      // push this CTA's sums into every CTA of the cluster (stores do not stall; the
+      // cluster barrier makes them visible), so step 2 reads only local shared memory
+      if (tid < 3 * (kDim / 2)) {
+        const int j = tid / 3, k = tid % 3;
+        const double v = (S.part4[0][j][k] + S.part4[1][j][k]) + (S.part4[2][j][k] + S.part4[3][j][k]);
+#pragma unroll
+        for (int c = 0; c < kJCtas; ++c) cluster.map_shared_rank(&S, c)->all[buf][rank][j][k] = v;
+      }
+      cluster.sync();
+      // (2) cluster sums and the rotation of each pair, four lanes per pair: lane c2 adds
+      // CTAs 2 c2 and 2 c2 + 1, a fixed shuffle tree adds the rest (the same order in
+      // every CTA, so every CTA derives the same rotations)
+      {
+        const int j = tid >> 2, c2 = tid & 3;
+        const double *x0 = S.all[buf][2 * c2][j], *x1 = S.all[buf][2 * c2 + 1][j];
+        double app = x0[0] + x1[0];
+        double aqq = x0[1] + x1[1];
+        double apq = x0[2] + x1[2];
+#pragma unroll
+        for (int m = 1; m <= 2; m <<= 1) {
+          app += __shfl_xor_sync(0xffffffffu, app, m);
+          aqq += __shfl_xor_sync(0xffffffffu, aqq, m);
+          apq += __shfl_xor_sync(0xffffffffu, apq, m);
+        }
+        if (!isfinite(app) || !isfinite(aqq) || !isfinite(apq)) sfin = false;
+        smax = fmax(smax, fabs(apq));
+        dmax = fmax(dmax, fmax(fabs(app), fabs(aqq)));
+        const double delta = (aqq - app) * 0.5;
+        const double sgn = delta >= 0.0 ? 1.0 : -1.0;
+        const double h2 = fma(delta, delta, apq * apq);
+        const double h = h2 > 0.0 ? h2 * rsqrt_f64(h2) : 0.0;
+        double tang = sgn * apq * rcp_f64(fmax(fabs(delta) + h, 1e-300));
+        if (!(fabs(apq) > 1e-8 * (fabs(app) + fabs(aqq)) + 1e-20)) tang = 0.0;
+        const double cs = rsqrt_f64(fma(tang, tang, 1.0));
+        if (c2 == 0) {
+          S.cs[j][0] = cs;
+          S.cs[j][1] = tang * cs;
+        }
+      }
+      __syncthreads();
+      // (3) rotate columns p, q of the local rows of W and V
       for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
         const int lr = e / (kDim / 2), j = e % (kDim / 2);
         int p, q;
         round_pair(j, r, p, q);
         const double c = S.cs[j][0], s = S.cs[j][1];
-        const double ap = S.a[lr][p], aq = S.a[lr][q];
-        S.nx[lr][p] = ap * c - aq * s;
-        S.nx[lr][q] = ap * s + aq * c;
+        const double wp = S.a[lr][p], wq = S.a[lr][q];
+        S.a[lr][p] = wp * c - wq * s;
+        S.a[lr][q] = wp * s + wq * c;
         const double up = S.u[lr][p], uq = S.u[lr][q];
         S.u[lr][p] = up * c - uq * s;
         S.u[lr][q] = up * s + uq * c;
       }
-      cluster.sync();
-      // (3) row rotations: each local row x of J^T (A J) from its own nx row and its
-      // partner's nx row y, read from y's owner (16-byte loads, independent and unrolled
-      // so that they are in flight together)
-#pragma unroll
-      for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
-        const int lr = e / (kDim / 2), c2 = e % (kDim / 2);
-        const int x = row0 + lr;
-        int y, j, isp;
-        if (x == kDim - 1) {
-          y = r, j = 0, isp = 1;
-        } else if (x == r) {
-          y = kDim - 1, j = 0, isp = 0;
-        } else {
-          y = mod_dm1(mod_dm1(2 * r - x));
-          const int jp = mod_dm1(x - r);  // x = (r + jp) mod (D-1)
-          if (jp >= 1 && jp < kDim / 2) {
-            j = jp, isp = 1;
-          } else {
-            j = mod_dm1(r - x), isp = 0;  // x = (r - j) mod (D-1)
-          }
-        }
-        const JacobiSmem *own = cluster.map_shared_rank(&S, y / kJRows);
-        const double2 by = reinterpret_cast<const double2 *>(own->nx[y % kJRows])[c2];
-        const double2 bx = reinterpret_cast<const double2 *>(S.nx[lr])[c2];
-        const double c = S.cs[j][0], s = S.cs[j][1];
-        double2 o;
-        o.x = isp ? (c * bx.x - s * by.x) : (s * by.x + c * bx.x);
-        o.y = isp ? (c * bx.y - s * by.y) : (s * by.y + c * bx.y);
-        reinterpret_cast<double2 *>(S.a[lr])[c2] = o;
-      }
-      cluster.sync();
+      __syncthreads();
+      buf ^= 1;
     }
     sweeps_done = sweep + 1;
-    if ((sweep + 1) % 2 == 0 || sweep + 1 == max_sweeps) {
-      // residual = max|offdiag| / max|diag| over the matrix (non-finite -> fail)
-      double off = 0.0, dg = 0.0;
-      bool fin = true;
-      for (int e = tid; e < kJRows * kDim; e += kJThreads) {
-        const int lr = e / kDim, col = e % kDim;
-        const double v = S.a[lr][col];
-        if (!isfinite(v)) fin = false;
-        if (col == row0 + lr) dg = fmax(dg, fabs(v));
-        else off = fmax(off, fabs(v));
-      }
+    // the sweep's residual (identical in every CTA: the same sums in the same order)
 #pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        off = fmax(off, __shfl_xor_sync(0xffffffffu, off, o));
-        dg = fmax(dg, __shfl_xor_sync(0xffffffffu, dg, o));
-      }
-      fin = __all_sync(0xffffffffu, fin);
-      if (lane == 0) wo[warp] = off, wd[warp] = dg, wf[warp] = fin;
-      __syncthreads();
-      if (tid == 0) {
-        double o = 0.0, d = 0.0;
-        int f = 1;
-        for (int q = 0; q < kJWarps; ++q) o = fmax(o, wo[q]), d = fmax(d, wd[q]), f &= wf[q];
-        S.stat[0] = o, S.stat[1] = d, S.flag[0] = f;
-      }
-      cluster.sync();
-      double o = 0.0, d = 0.0;
-      int f = 1;
-      for (int q = 0; q < kJCtas; ++q) {
-        const JacobiSmem *other = cluster.map_shared_rank(&S, q);
-        o = fmax(o, other->stat[0]);
-        d = fmax(d, other->stat[1]);
-        f &= other->flag[0];
-      }
-      finite = f != 0 && isfinite(o) && isfinite(d);
-      residual = finite ? o / fmax(d, 1e-30) : INFINITY;
-      cluster.sync();
-      if (!finite || residual < (double)tol) break;
+    for (int o = 16; o; o >>= 1) {
+      smax = fmax(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+      dmax = fmax(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
     }
+    sfin = __all_sync(0xffffffffu, sfin);
+    if (lane == 0) wo[warp] = smax, wd[warp] = dmax, wf[warp] = sfin;
+    __syncthreads();
+    double o = 0.0, d = 0.0;
+    int f = 1;
+    for (int w = 0; w < kJWarps; ++w) o = fmax(o, wo[w]), d = fmax(d, wd[w]), f &= wf[w];
+    __syncthreads();
+    finite = f != 0 && isfinite(o) && isfinite(d);
+    residual = finite ? o / fmax(d, 1e-300) : INFINITY;
+    if (!finite || residual < (double)tol) break;
   }
-  // eigenvalues: gather the diagonal, rank ascending (ties by index)
-  if (tid < kJRows) S.nx[0][row0 + tid] = S.a[tid][row0 + tid];
+  // eigenvalues: Rayleigh quotients v_p . w_p, summed over the cluster's rows
+  for (int i = tid; i < kDim; i += kJThreads) {
+    double acc = 0.0;
+    for (int lr = 0; lr < kJRows; ++lr) acc = fma(S.u[lr][i], S.a[lr][i], acc);
+    S.evpart[i] = acc;
+  }
   cluster.sync();
   for (int i = tid; i < kDim; i += kJThreads) {
-    const JacobiSmem *own = cluster.map_shared_rank(&S, i / kJRows);
-    S.diag[i] = own->nx[0][i];
+    double acc = 0.0;
+    for (int c = 0; c < kJCtas; ++c) acc += cluster.map_shared_rank(&S, c)->evpart[i];
+    S.diag[i] = acc;
   }
   cluster.sync();
   for (int i = tid; i < kDim; i += kJThreads) {
@@ -458,13 +475,13 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
   // sorted U rows (local), Hadamard butterfly, bit-reversed placement, / sqrt(256)
   for (int e = tid; e < kJRows * kDim; e += kJThreads) {
     const int lr = e / kDim, i = e % kDim;
-    S.nx[lr][rank_of[i]] = S.u[lr][i];
+    S.a[lr][rank_of[i]] = S.u[lr][i];
   }
   __syncthreads();
   for (int lr = warp; lr < kJRows; lr += kJWarps) {
     double v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = S.nx[lr][8 * lane + e];
+    for (int e = 0; e < 8; ++e) v[e] = S.a[lr][8 * lane + e];
 #pragma unroll
     for (int bit = 0; bit < 3; ++bit) {
       double nv[8];
