@@ -290,6 +290,7 @@ def traffic_per_launch(requests):
 
 
 TARGET_REGION_S = 3.0  # each timed leg runs about this long, whatever --steps is
+MIN_HEADS_PER_RANK = 2
 
 
 def run_gpu(args):
@@ -311,10 +312,12 @@ def run_gpu(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     _lib.lib()
     # One global batch of B * world config-3 requests, split by KV head (tensor parallel,
-    # as the model shards its heads) and then by request: every rank gets B * tp requests
-    # x H / tp KV heads, the per-GPU work of N = 1.
-    tp = head_split(H, world)
-    shard = shard_of(rank, [SEQ] * (B * world), H, world)
+    # as the model shards its heads) down to 2 KV heads per rank, then by request: every
+    # rank gets B * tp requests x H / tp KV heads, the per-GPU work of N = 1.  (On one
+    # B200 a 128-request x 2-head shard runs a forward in 510 us like 64 x 4, a 256 x 1
+    # shard in 557 us: the raw path and the merges grow with the requests.)
+    tp = head_split(H, world, MIN_HEADS_PER_RANK)
+    shard = shard_of(rank, [SEQ] * (B * world), H, world, MIN_HEADS_PER_RANK)
     st = build_state(device, seed=1234 + rank, requests=len(shard.requests), kv_heads=shard.kv_heads)
     nr, h = st["requests"], st["kv_heads"]
     sizes = workload_sizes(nr, h)

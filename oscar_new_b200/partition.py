@@ -35,11 +35,17 @@ class Shard:
         return range(self.head_begin * group, self.head_end * group)
 
 
-def head_split(kv_heads: int, world: int) -> int:
-    """Tensor-parallel degree over KV heads: the largest divisor of both."""
-    if kv_heads <= 0 or world <= 0:
-        raise ValueError("kv_heads and world must be positive")
-    return math.gcd(kv_heads, world)
+def head_split(kv_heads: int, world: int, min_heads_per_rank: int = 1) -> int:
+    """Tensor-parallel degree over KV heads: the largest common divisor of both that
+    leaves every rank at least `min_heads_per_rank` KV heads (1: the model's TP split)."""
+    if kv_heads <= 0 or world <= 0 or min_heads_per_rank <= 0:
+        raise ValueError("kv_heads, world and min_heads_per_rank must be positive")
+    g = math.gcd(kv_heads, world)
+    while g > 1 and kv_heads // g < min_heads_per_rank:
+        g -= 1
+        while g > 1 and (kv_heads % g or world % g):
+            g -= 1
+    return g
 
 
 def balance_requests(context_lens, groups: int) -> list:
@@ -59,16 +65,16 @@ def balance_requests(context_lens, groups: int) -> list:
     return [sorted(m) for m in members]
 
 
-def partition(context_lens, kv_heads: int, world: int) -> list:
+def partition(context_lens, kv_heads: int, world: int, min_heads_per_rank: int = 1) -> list:
     """The shard of every rank: rank = request_group * tp + head_group."""
-    tp = head_split(kv_heads, world)
+    tp = head_split(kv_heads, world, min_heads_per_rank)
     per = kv_heads // tp
     groups = balance_requests(context_lens, world // tp)
     return [Shard(rank=g * tp + h, head_begin=h * per, head_end=(h + 1) * per, requests=tuple(groups[g]))
             for g in range(world // tp) for h in range(tp)]
 
 
-def shard_of(rank: int, context_lens, kv_heads: int, world: int) -> Shard:
+def shard_of(rank: int, context_lens, kv_heads: int, world: int, min_heads_per_rank: int = 1) -> Shard:
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world {world}")
-    return partition(context_lens, kv_heads, world)[rank]
+    return partition(context_lens, kv_heads, world, min_heads_per_rank)[rank]

@@ -37,6 +37,12 @@ def test_every_request_head_pair_has_exactly_one_rank(world, kv_heads):
 
 def test_heads_split_first_then_requests():
     assert [head_split(4, w) for w in (1, 2, 4, 8)] == [1, 2, 4, 4]
+    assert [head_split(4, w, 2) for w in (1, 2, 4, 8)] == [1, 2, 2, 2]
+    assert [head_split(8, w, 2) for w in (1, 2, 4, 8)] == [1, 2, 4, 4]
+    assert head_split(6, 6, 2) == 3 and head_split(6, 4, 2) == 2
+    shards = partition([100] * 8, 4, 8, 2)  # TP2 x 4 request groups
+    assert {(s.head_begin, s.head_end) for s in shards} == {(0, 2), (2, 4)}
+    assert len({s.requests for s in shards}) == 4
     shards = partition([100] * 8, 4, 8)  # TP4 (one KV head per rank) x 2 request groups
     assert [(s.head_begin, s.head_end) for s in shards[:4]] == [(0, 1), (1, 2), (2, 3), (3, 4)]
     assert shards[0].requests == shards[3].requests and not set(shards[0].requests) & set(shards[4].requests)
