@@ -40,6 +40,34 @@ def test_invalid_arguments_are_rejected_without_launch():
     assert handle.oscar_rotate(None, 0, 1, 0, 0, 1, None, 0, 0, None, None) == 1
 
 
+def test_metadata_staging_rejects_inconsistent_steps_without_launch():
+    """oscar_stage_step_metadata checks the step against the arena before any device
+    work: more requests / tokens / columns than the arena holds, missing sources."""
+    h = _lib.lib()
+    fake = 1 << 20  # never dereferenced: every call below is refused first
+    args = dict(qs=fake, sl=fake, tb=fake, ts=40, sm=fake, nr=3, nt=3, cc=17, tile=4, arena=fake, mr=5, cols=39,
+                cap=19, so=fake, scap=40)
+
+    def call(**kw):
+        a = {**args, **kw}
+        return h.oscar_stage_step_metadata(a["qs"], a["sl"], a["tb"], a["ts"], a["sm"], a["nr"], a["nt"], a["cc"],
+                                           a["tile"], a["arena"], a["mr"], a["cols"], a["cap"], a["so"], a["scap"],
+                                           None)
+
+    assert call(nr=6) == 1              # more requests than the arena
+    assert call(nt=41) == 1             # more tokens than the slot buffer
+    assert call(cc=40) == 1             # more columns than the table
+    assert call(qs=None) == 1           # requests without query starts
+    assert call(sm=None) == 1           # tokens without a slot mapping
+    assert call(ts=10) == 1             # a source row shorter than the columns copied
+    assert call(arena=None) == 1
+    assert call(tile=0) == 1
+    offsets = (ctypes.c_int64 * 5)()
+    assert h.oscar_step_arena_layout(0, 39, 19, ctypes.addressof(offsets)) == 1
+    assert h.oscar_step_arena_layout(5, 39, 19, ctypes.addressof(offsets)) == 0
+    assert list(offsets) == [4, 12, 20, 216, 256]
+
+
 def test_sst_weights_reject_keys_that_are_not_16_byte_rows():
     """The SST entry points read key rows as 16-byte vectors: a key pointer off a 16-byte
     boundary or strides that are not multiples of 8 elements are refused before any
