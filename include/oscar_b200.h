@@ -87,6 +87,18 @@ int oscar_version(void);
  * an error status, not a hang, and that the context stays usable. */
 int oscar_selftest_bounded_wait(int32_t *status, void *stream);
 
+/* Causal BF16 attention of a first prefill (every request starts at position 0): the
+ * current tokens only, D = 256, grouped-query heads (hq a multiple of hkv), variable
+ * lengths from the device query starts [num_reqs + 1]; max_query_len is the host bound
+ * that sizes the grid.  query [n, hq, 256], key / value [n, hkv, 256] bf16 rows with
+ * element strides (token, head) that are multiples of 8; out [n, hq, 256] bf16.  A
+ * tcgen05 kernel of this library where the reference hands the case to the vendor's fused
+ * attention (backend.py:175-193). */
+int oscar_prefill_attention(const void *query, int64_t qs0, int64_t qs1, const void *key, int64_t ks0, int64_t ks1,
+                            const void *value, int64_t vs0, int64_t vs1, const int32_t *qstarts, int32_t num_reqs,
+                            int32_t max_query_len, int64_t n, int32_t hq, int32_t hkv, float scale, void *out,
+                            int64_t os0, int64_t os1, int32_t *status, void *stream);
+
 /* Which history kernel the latest successful history launch of this process used
  * (a host-side record made at launch time; no device access): 0 none yet,
  * OSCAR_HISTORY_ATTENTION_KERNEL (mma.sync, decode and general rows),

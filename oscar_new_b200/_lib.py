@@ -54,6 +54,8 @@ _SIGNATURES = {
     "oscar_selftest_bounded_wait": [P, P],
     "oscar_test_set_wait_fault": [I32, C.c_uint32],
     "oscar_last_history_kernel": [],
+    "oscar_prefill_attention": [P, I64, I64, P, I64, I64, P, I64, I64, P, I32, I32, I64, I32, I32, F32, P, I64, I64, P,
+                                P],
     "oscar_rotate": [P, I64, I32, I64, I64, I64, P, I64, I64, P, P],
     "oscar_store_int2": [P, P, I64, P, P, P, Geometry, Clip, Clip, P],
     "oscar_rotate_store": [P, I64, I64, P, I64, I64, I64, P, P, P, P, P, Geometry, Clip, Clip, P, I64, I64, I32, P, P, P, P, P],

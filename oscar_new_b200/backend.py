@@ -160,30 +160,19 @@ class OscarAttentionImpl(AttentionImpl):
     def _first_prefill(self, query, key, value, meta, output):
         """Requests that start at position 0: the cache gets the same INT2 history and
         BF16 window writes as on the general path; attention is causal over the current
-        bf16 K/V only, computed by torch's flash-attention kernel (a library call, like
-        the reference's vendor fused attention for this case)."""
-        import torch.nn.functional as F
-        from torch.nn.attention import SDPBackend, sdpa_kernel
-
+        bf16 K/V only, computed by this library's tcgen05 prefill kernel (the reference
+        hands this case to the vendor's fused attention, backend.py:175-193)."""
         from . import kernels
 
         kernels.rotate_store(key, value, self.rk, self.rv, self.history, meta.slot_mapping, meta.counts,
                              meta.layout)
         out = output.view(-1, self.num_heads, self.head_size)
-        starts = meta.query_start_loc_cpu.tolist()
-        with sdpa_kernel([SDPBackend.FLASH_ATTENTION]):
-            for i in range(meta.num_reqs):
-                a, b = starts[i], starts[i + 1]
-                if b == a:
-                    continue
-                o = F.scaled_dot_product_attention(query[a:b].transpose(0, 1).unsqueeze(0),
-                                                   key[a:b].transpose(0, 1).unsqueeze(0),
-                                                   value[a:b].transpose(0, 1).unsqueeze(0), is_causal=True,
-                                                   enable_gqa=True, scale=self.scale)
-                out[a:b].copy_(o[0].transpose(0, 1))
+        end = int(meta.query_start_loc_cpu[meta.num_reqs])
+        kernels.prefill_attention(query, key, value, meta.query_start_loc, meta.num_reqs, meta.max_query_len,
+                                  self.scale, out[:end])
         # rows past the step's last request are padding (graph-sized batches): zero, as
         # the reference does after its fused prefill attention
-        out[starts[meta.num_reqs]:].zero_()
+        out[end:].zero_()
         kernels.store_windows(key, value, self.window, meta, meta.layout)
         return output
 

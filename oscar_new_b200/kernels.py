@@ -234,6 +234,25 @@ def stage_step_metadata(arena, slot_out, max_reqs, columns, task_capacity, query
               _stream(arena))
 
 
+def prefill_attention(query, key, value, query_start_loc, num_reqs: int, max_query_len: int, scale: float,
+                      out=None):
+    """Causal attention of a first prefill over the current tokens only (tcgen05 kernel):
+    query [n, Hq, 256], key / value [n, Hkv, 256] bf16, device query starts
+    [num_reqs + 1]; returns / fills out [n, Hq, 256] bf16."""
+    _require_cuda(query, key, value, query_start_loc, out)
+    n, hq, d = query.shape
+    if out is None:
+        out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=query.device)
+    if n == 0 or num_reqs == 0:
+        return out
+    query, key, value = _rows(query), _rows(key), _rows(value)
+    _lib.call("oscar_prefill_attention", query.data_ptr(), query.stride(0), query.stride(1), key.data_ptr(),
+              key.stride(0), key.stride(1), value.data_ptr(), value.stride(0), value.stride(1),
+              query_start_loc.data_ptr(), num_reqs, max_query_len, n, hq, key.shape[1], float(scale), out.data_ptr(),
+              out.stride(0), out.stride(1), _status(out), _stream(query))
+    return out
+
+
 def _meta_common(meta, layout, hq):
     geo = geometry(layout, hq, meta.block_tables.stride(0))
     if meta.block_tables.stride(1) != 1:

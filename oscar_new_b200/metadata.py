@@ -112,9 +112,9 @@ class OscarMetadata:
     layout: CacheLayout
     is_dummy: bool = False
     # host query starts when every request of the step is a first prefill (no history,
-    # no window yet); the forward then hands the causal attention to a library
-    # flash-attention kernel (the reference hands it to the vendor's fused attention,
-    # backend.py:175-193)
+    # no window yet); the forward then runs the causal attention over the current tokens
+    # with the tcgen05 prefill kernel (the reference hands it to the vendor's fused
+    # attention, backend.py:175-193)
     prefill_starts: torch.Tensor | None = None
     causal: bool = True
 

@@ -102,10 +102,10 @@ def test_impl_forward_replays_from_graph_captured_as_dummy(cuda_lib, oscar_env):
     del graph
 
 
-def test_first_prefill_uses_flash_path_and_writes_the_same_cache(cuda_lib, oscar_env, monkeypatch):
+def test_first_prefill_uses_the_prefill_kernel_and_writes_the_same_cache(cuda_lib, oscar_env, monkeypatch):
     """A batch whose host length bound equals its query lengths (no history yet) runs
-    the library flash-attention route; the same batch without the bound runs the
-    general path.  Outputs match the dense oracle; the caches are byte-identical."""
+    the tcgen05 prefill kernel; the same batch without the bound runs the general path.
+    Outputs match the dense oracle; the caches are byte-identical."""
     _, impl, _ = oscar_env
     vc = fake_vllm_config(scheduler_config=SimpleNamespace(max_num_seqs=3, max_num_batched_tokens=2048),
                           speculative_config=SimpleNamespace(num_speculative_tokens=3))

@@ -45,7 +45,7 @@ def test_vllm_engine_generates_through_oscar(cuda_lib, mode):
 
 def test_first_token_matches_the_native_backend(cuda_lib):
     """The first generated token comes from the prefill forward, which OSCAR runs through
-    a library flash-attention kernel over the exact BF16 current K/V while it writes the
+    the tcgen05 prefill kernel over the exact BF16 current K/V while it writes the
     INT2 history and the window: it must equal the native backend's.  Later tokens read
     the INT2 history and may differ (a random-weight model has nearly flat logits)."""
     native = run_engine("eager", oscar=0)
