@@ -1072,6 +1072,19 @@ def profile_only(what):
         torch.cuda.synchronize(device)
         print("profile run done: config 4 (8 requests) history")
         return
+    if what == "prefill":
+        # first prefill of one 8192-token request, 24 query / 4 KV heads (tcgen05 kernel)
+        gen = torch.Generator(device=device).manual_seed(8)
+        n = 8192
+        q = torch.randn(n, H * G, D, device=device, generator=gen).bfloat16()
+        k = torch.randn(n, H, D, device=device, generator=gen).bfloat16()
+        v = torch.randn(n, H, D, device=device, generator=gen).bfloat16()
+        starts = torch.tensor([0, n], dtype=torch.int32, device=device)
+        for _ in range(4):
+            kernels.prefill_attention(q, k, v, starts, 1, n, 1.0 / math.sqrt(D))
+        torch.cuda.synchronize(device)
+        print("profile run done: prefill 8192 tokens")
+        return
     if what == "rotate-store":
         cs = config2_state(device)
         for _ in range(4):
@@ -1115,8 +1128,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=B, help="requests per GPU (profiling runs use fewer)")
-    ap.add_argument("--profile-kernel", choices=["history", "step", "forward", "rotate-store", "mtp-verify",
-                                                 "calibration"],
+    ap.add_argument("--profile-kernel", choices=["history", "step", "forward", "prefill", "rotate-store",
+                                                 "mtp-verify", "calibration"],
                     default=None,
                     help="build the state, run 4 launches of the kernel (or 4 layer steps) and exit")
     ap.add_argument("--workload", choices=["decode", "rotate-store", "mtp-verify", "calibration"], default="decode",

@@ -168,8 +168,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(const 
       if (!ok) break;
       tc_fence_after();
       uint32_t a[32], b[32];
-      tmem_load32(lane_base + kColS + 64 * s, a);
-      tmem_load32(lane_base + kColS + 64 * s + 32, b);
+      tmem_load32x2(lane_base + kColS + 64 * s, a, lane_base + kColS + 64 * s + 32, b);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.s_empty[s]);
@@ -183,9 +182,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(const 
         for (int c = 0; c < 64; ++c)
           if (j * kPfK + c > qi) x[c] = -INFINITY;
       }
-      float bmax = x[0];
+      // tree reductions: no 64-long dependency chain
+      float t32[32];
 #pragma unroll
-      for (int c = 1; c < 64; ++c) bmax = fmaxf(bmax, x[c]);
+      for (int c = 0; c < 32; ++c) t32[c] = fmaxf(x[c], x[c + 32]);
+#pragma unroll
+      for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+        for (int c = 0; c < w; ++c) t32[c] = fmaxf(t32[c], t32[c + w]);
+      const float bmax = t32[0];
       const bool rebase = m != -INFINITY && bmax > m + kPfSlack;
       if (m == -INFINITY) m = bmax;
       if (__any_sync(0xffffffffu, rebase)) {
@@ -210,14 +215,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attention_kernel(const 
         }
       }
       uint32_t pk[32];
-      float sum = 0.f;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const float p0 = ex2(x[2 * c] - m), p1 = ex2(x[2 * c + 1] - m);
-        sum += p0 + p1;
+        acc[c & 3] += p0 + p1;
         pk[c] = pack_bf162(p0, p1);
       }
-      l += sum;
+      l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
       // P buffer s was read by P V of block j - 2
       if (j >= 2 && !pf_wait(&S.pv_done[s], ((j - 2) >> 1) & 1, S)) {
         ok = false;
