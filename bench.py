@@ -772,25 +772,35 @@ def run_rotate_store(args):
     print(json.dumps(line), flush=True)
 
 
-def config4_state(device, seed=404, nreq=32):
+def config4_contexts(seed=404):
+    """The 32 context lengths of config 4: exp(U(ln 2048, ln 262144)), seeded."""
+    gen = torch.Generator().manual_seed(seed)
+    u = torch.rand(32, generator=gen, dtype=torch.float64)
+    return [int(math.exp(math.log(2048) + x * (math.log(262144) - math.log(2048)))) for x in u.tolist()]
+
+
+def config4_state(device, seed=404, nreq=32, requests=None, kv_heads=None):
     """Config 4 (MTP verify): 32 requests with qlen 4 (1 + 3 draft tokens) and seq_len
-    ~ exp(U(ln 2048, ln 262144)) seeded; S=4, R=128, MTP=3; request 5's last draft has
-    a padded -1 slot and a 33rd, zero-length padded row closes the batch.  ``nreq`` < 32
-    keeps the first requests only (small ncu captures)."""
+    ~ exp(U(ln 2048, ln 262144)) seeded; S=4, R=128, MTP=3; the sixth request's last
+    draft has a padded -1 slot and a zero-length padded row closes the batch.  ``nreq``
+    < 32 keeps the first requests only (small ncu captures); ``requests`` / ``kv_heads``
+    build one rank's shard (its requests, its number of KV heads)."""
     from oscar_new_b200 import kernels
     from oscar_new_b200.config import OscarConfig
     from oscar_new_b200.layout import CacheLayout
     from oscar_new_b200.synthetic import cache_stripes, plan_pages, rotation
 
-    gen = torch.Generator().manual_seed(seed)
-    u = torch.rand(32, generator=gen, dtype=torch.float64)
-    seqs = [int(math.exp(math.log(2048) + x * (math.log(262144) - math.log(2048)))) for x in u.tolist()][:nreq]
+    all_seqs = config4_contexts(seed)
+    chosen = list(range(nreq)) if requests is None else list(requests)
+    seqs = [all_seqs[r] for r in chosen]
+    nreq = len(seqs)
+    h = H if kv_heads is None else kv_heads
     seqs.append(0)
     qlens = [4] * nreq + [0]
     cfg = replace(OscarConfig(), sink_tokens=SINK, recent_tokens=RECENT, speculative_tokens=3)
-    layout = CacheLayout(BP, kv_heads=H, config=cfg)
-    plan = plan_pages(seqs, qlens, BP, seed=seed, max_reqs=34)
-    cache = cache_stripes(plan.num_pages, BP, H, device)
+    layout = CacheLayout(BP, kv_heads=h, config=cfg)
+    plan = plan_pages(seqs, qlens, BP, seed=seed, max_reqs=nreq + 2)
+    cache = cache_stripes(plan.num_pages, BP, h, device)
     history, window = layout.tensor_views(cache)
     rk, rv = rotation(1).bfloat16().to(device), rotation(2).bfloat16().to(device)
     dgen = torch.Generator(device=device).manual_seed(seed)
@@ -799,10 +809,10 @@ def config4_state(device, seed=404, nreq=32):
         prefix = sq - ql
         for s0 in range(0, prefix, chunk):
             n = min(chunk, prefix - s0)
-            k = torch.randn(n, H, D, device=device, generator=dgen)
+            k = torch.randn(n, h, D, device=device, generator=dgen)
             k[..., :8] *= 20
             k = k.bfloat16()
-            v = torch.randn(n, H, D, device=device, generator=dgen).bfloat16()
+            v = torch.randn(n, h, D, device=device, generator=dgen).bfloat16()
             slots = plan.slots_of(req, range(s0, s0 + n)).to(device)
             counts = torch.tensor([1, n], dtype=torch.int32, device=device)
             kernels.rotate_store(k, v, rk, rv, history, slots, counts, layout)
@@ -817,34 +827,65 @@ def config4_state(device, seed=404, nreq=32):
     if nreq > 5:
         meta.slot_mapping[5 * 4 + 3] = -1
     t = sum(qlens)
-    q = torch.randn(t, H * G, D, device=device, generator=dgen).bfloat16()
-    k = torch.randn(t, H, D, device=device, generator=dgen)
+    q = torch.randn(t, h * G, D, device=device, generator=dgen).bfloat16()
+    k = torch.randn(t, h, D, device=device, generator=dgen)
     k[..., :8] *= 20
-    v = torch.randn(t, H, D, device=device, generator=dgen).bfloat16()
+    v = torch.randn(t, h, D, device=device, generator=dgen).bfloat16()
     torch.cuda.synchronize(device)
     hist_heads = 0
     for sq, ql in zip(seqs, qlens):
         prefix = sq - ql
         sink_len = min(SINK, prefix)
-        hist_heads += H * max(0, max(sink_len, prefix - RECENT) - sink_len)
+        hist_heads += h * max(0, max(sink_len, prefix - RECENT) - sink_len)
     return dict(cfg=cfg, layout=layout, plan=plan, cache=cache, history=history, window=window, rk=rk, rv=rv,
-                meta=meta, q=q, k=k.bfloat16(), v=v, seqs=seqs, qlens=qlens, hist_token_heads=hist_heads)
+                meta=meta, q=q, k=k.bfloat16(), v=v, seqs=seqs, qlens=qlens, hist_token_heads=hist_heads, kv_heads=h,
+                requests=nreq)
 
 
 def run_mtp_verify(args):
+    """Config 4 on N GPUs: the fixed batch of 32 requests split by KV head (at least 2 per
+    rank) and by request, balanced by total context (partition.py); strong scaling."""
     from oscar_new_b200 import _lib, kernels
     from oscar_new_b200.config import decode_split_cap
+    from oscar_new_b200.partition import head_split, shard_of
 
-    device = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     _lib.lib()
-    st = config4_state(device)
+    contexts = config4_contexts()
+    tp = head_split(H, world, MIN_HEADS_PER_RANK)
+    shard = shard_of(rank, contexts, H, world, MIN_HEADS_PER_RANK)
+    st = config4_state(device, requests=shard.requests, kv_heads=shard.kv_heads)
+    h, nr = st["kv_heads"], st["requests"]
     m = st["meta"]
     t = st["q"].shape[0]
-    splits = decode_split_cap(32, H, 4, t, H * G)
-    out = torch.empty((t, H * G * D), dtype=torch.bfloat16, device=device)
-    scratch = kernels.DecodeScratch(t, H * G, splits, device)
+    splits = decode_split_cap(nr, h, 4, t, h * G)
+    out = torch.empty((t, h * G * D), dtype=torch.bfloat16, device=device)
+    scratch = kernels.DecodeScratch(t, h * G, splits, device)
     scale = 1.0 / math.sqrt(D)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        v = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        return float(v.item())
 
     def step():
         kernels.prepare_tasks(m.query_start_loc, m.counts, m.tasks, m.task_count, m.max_num_reqs,
@@ -854,51 +895,61 @@ def run_mtp_verify(args):
         kernels.decode_attention(qrot, st["q"], st["k"], st["v"], st["history"], st["window"], m, st["layout"],
                                  scale, splits, st["rv"], out, scratch)
 
-    stream = torch.cuda.current_stream(device)
+    def timed(fn, steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device) as clocks:
         t0 = time.time()
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
+        ms = timed(step, args.steps)
         clocks.mark(t0, time.time())
-    ms = e0.elapsed_time(e1) / args.steps
     qrot = kernels.rotate(st["q"], st["rk"])
+
+    def history():
+        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"], scale,
+                                   splits, False)
+
     for _ in range(3):
-        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"], scale,
-                                   splits, False)
-    torch.cuda.synchronize(device)
-    e0.record(stream)
-    for _ in range(args.steps):
-        kernels.attention_partials(qrot, st["k"], st["v"], st["history"], st["window"], m, st["layout"], scale,
-                                   splits, False)
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    kern_ms = e0.elapsed_time(e1) / args.steps
+        history()
+    kern_ms = timed(history, args.steps)
     hist_bytes = st["hist_token_heads"] * HISTORY_BYTES_PER_TOKEN_HEAD
-    kv_tokens = sum(st["seqs"]) * H
-    peak, peak_kind = measured_peaks()
-    achieved = hist_bytes / (kern_ms * 1e-3) / 1e9
-    line = {
-        "metric": METRIC, "value": kv_tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int2-kv/bf16", "data": "synthetic (seeded, config 4)",
-        "config": {"workload": "config4 MTP verify (qlen 4) paged INT2 decode attention layer",
-                   "requests": 32, "padded_rows": 1, "sum_seq_len": sum(st["seqs"]),
-                   "kv_splits": f"balanced per request, at most {splits}",
-                   "history_token_heads": st["hist_token_heads"], "history_bytes": hist_bytes,
-                   "l2": "inputs larger than L2", "us_per_layer": ms * 1e3},
-        "roofline": {"kernel": "history_attention_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
-                     "peak_kind": f"{peak_kind} hbm copy GB/s", "unit": "GB/s", "frac": achieved / peak,
-                     "us_per_launch": kern_ms * 1e3, "algorithmic_bytes_per_launch": hist_bytes, "traffic": None},
-        "gpu_launches": 6 * args.steps, "clocks": clocks.summary(),
-    }
-    print(json.dumps(line), flush=True)
+    total_kv = sum(contexts) * H
+    own_ctx = sum(contexts[r] for r in shard.requests)
+    ctx_max = max_over_ranks(float(own_ctx * shard.kv_heads))
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = hist_bytes / (kern_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": total_kv / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int2-kv/bf16", "data": "synthetic (seeded, config 4)",
+            "config": {"workload": "config4 MTP verify (qlen 4) paged INT2 decode attention layer",
+                       "requests": 32, "padded_rows": 1, "sum_seq_len": sum(contexts),
+                       "partition": f"KV heads tensor-parallel x{tp}, requests x{world // tp} balanced by context "
+                                    f"(partition.py); rank 0: {nr} requests x {h} KV heads",
+                       "kv_heads_x_context_max_over_ranks_vs_mean": ctx_max / (total_kv / world),
+                       "kv_splits": f"balanced per request, at most {splits}",
+                       "history_token_heads_rank0": st["hist_token_heads"], "l2": "inputs larger than L2",
+                       "us_per_layer": ms * 1e3},
+            "roofline": {"kernel": "history_mtp_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                         "peak_kind": f"{peak_kind} hbm copy GB/s", "unit": "GB/s", "frac": achieved / peak,
+                         "us_per_launch": kern_ms * 1e3, "algorithmic_bytes_per_launch": hist_bytes,
+                         "traffic": None, "traffic_source": "not measured in this run (see profiles/)"},
+            "gpu_launches": 6 * args.steps, "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del scratch
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_calibration(args):
