@@ -286,6 +286,19 @@ int oscar_accumulate_gram_grouped(const void *x, int64_t n, int32_t h, int64_t x
 int oscar_sst_weights_per_head(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1,
                                const float *q_covs, float *weights, float *totals, void *stream);
 
+/* parts (bf16 [matrices][3][256][256], 16-byte aligned) = three bf16 matrices whose sum
+ * is each fp32 256x256 matrix of x exactly (hi, mid, lo).  Used once per calibration
+ * pass to prepare the query covariances for oscar_sst_weights_split. */
+int oscar_split_bf16x3(const float *x, int32_t matrices, void *parts, void *stream);
+
+/* oscar_sst_weights_per_head from pre-split covariances (parts of h matrices, as made by
+ * oscar_split_bf16x3) on the tcgen05 tensor cores; the same weights up to the order of
+ * the fp32 additions.  OSCAR_ERR_UNSUPPORTED when the key layout does not fit a tensor
+ * map (the caller then uses oscar_sst_weights_per_head); status (nullable) receives
+ * OSCAR_ERR_TIMEOUT if a device wait gave up. */
+int oscar_sst_weights_split(const void *key, int64_t n, int32_t h, int64_t ks0, int64_t ks1, const void *parts,
+                            float *weights, float *totals, int32_t *status, void *stream);
+
 /* out = x / max(denominator, 1e-30); the denominator is *device_denominator when
  * non-null, else host_denominator.  Reference :129-156. */
 int oscar_normalize(const float *x, int64_t numel, const float *device_denominator,

@@ -13,6 +13,7 @@ _PATH = Path(__file__).resolve().parent / "liboscar_b200.so"
 _lib = None
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "launch error", 3: "unsupported", 4: "device wait timeout"}
+UNSUPPORTED = 3  # OSCAR_ERR_UNSUPPORTED: the caller may take another path
 
 
 class Geometry(C.Structure):
@@ -72,6 +73,8 @@ _SIGNATURES = {
     "oscar_sst_weights": [P, I64, I32, I64, I64, P, P, P, P],
     "oscar_accumulate_gram_grouped": [P, I64, I32, I64, I64, I32, P, P, P],
     "oscar_sst_weights_per_head": [P, I64, I32, I64, I64, P, P, P, P],
+    "oscar_split_bf16x3": [P, I32, P, P],
+    "oscar_sst_weights_split": [P, I64, I32, I64, I64, P, P, P, P, P],
     "oscar_normalize": [P, I64, P, F32, P, P],
     "oscar_jacobi_rotations": [P, I32, I32, F32, P, P, P, P],
     "oscar_decode_attention_noalloc": [P, P, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, P, P, P, P, I32, I64, P, P, Geometry, F32, I32, I32, P, P],

@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "liboscar_b200.so"
 SOURCES = ["store.cu", "rotate_tc.cu", "attention.cu", "history_f8.cu", "history_mtp.cu", "calibration.cu",
-           "noalloc.cu", "metadata.cu", "gram_tc.cu",
+           "noalloc.cu", "metadata.cu", "gram_tc.cu", "sst_tc.cu",
            "prefill.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+from .kernels import status_word
 
 
 def _stream(t):
@@ -66,17 +67,43 @@ def accumulate_gram_grouped(x: torch.Tensor, covariances: torch.Tensor, weights:
               None if w is None else w.data_ptr(), covariances.data_ptr(), _stream(x))
 
 
-def sst_weights_per_head(key: torch.Tensor, q_covariances: torch.Tensor, totals: torch.Tensor):
+def prepare_sst_covariances(q_covariances: torch.Tensor) -> torch.Tensor:
+    """The three bf16 parts (hi, mid, lo; their sum is each fp32 entry exactly) of every
+    query covariance [h, 256, 256], as bf16 [h, 3, 256, 256]: computed once per
+    calibration pass and reused by every :func:`sst_weights_per_head` call of it."""
+    _cuda(q_covariances)
+    c = q_covariances.float().contiguous()
+    if c.dim() != 3 or c.shape[1:] != (256, 256):
+        raise ValueError("query covariances must be [h, 256, 256]")
+    parts = torch.empty((c.shape[0], 3, 256, 256), dtype=torch.bfloat16, device=c.device)
+    _lib.call("oscar_split_bf16x3", c.data_ptr(), c.shape[0], parts.data_ptr(), _stream(c))
+    return parts
+
+
+def sst_weights_per_head(key: torch.Tensor, q_covariances: torch.Tensor, totals: torch.Tensor,
+                         prepared: torch.Tensor | None = None):
     """Per-head ``w = max(k C_h k^T, 0)`` (key [n, h, 256], q_covariances [h, 256, 256])
-    and ``totals[h] += sum w``; returns w as fp32 [n * h] (token-major)."""
+    and ``totals[h] += sum w``; returns w as fp32 [n * h] (token-major).  With
+    ``prepared`` (:func:`prepare_sst_covariances` of the same covariances) the weights
+    come from the tcgen05 kernel, else (or when the key layout does not fit a tensor
+    map) from the mma.sync kernel, which splits the covariances itself."""
     _cuda(key, q_covariances, totals)
     n, h, d = key.shape
     if q_covariances.shape != (h, 256, 256) or totals.numel() != h or not totals.is_contiguous():
         raise ValueError("one covariance and one total per head")
     if key.dtype != torch.bfloat16 or key.stride(2) != 1 or key.stride(0) % 8 or key.stride(1) % 8 or key.data_ptr() % 16:
         key = key.to(torch.bfloat16).contiguous()
-    c = q_covariances.float().contiguous()
     weights = torch.empty(n * h, device=key.device, dtype=torch.float32)
+    if prepared is not None:
+        if prepared.shape != (h, 3, 256, 256) or prepared.dtype != torch.bfloat16 or not prepared.is_contiguous():
+            raise ValueError("prepared covariances must come from prepare_sst_covariances")
+        rc = _lib.lib().oscar_sst_weights_split(key.data_ptr(), n, h, key.stride(0), key.stride(1),
+                                                prepared.data_ptr(), weights.data_ptr(), totals.data_ptr(),
+                                                status_word(key.device).data_ptr(), _stream(key))
+        if rc != _lib.UNSUPPORTED:
+            _lib.check(rc, "oscar_sst_weights_split")
+            return weights
+    c = q_covariances.float().contiguous()
     _lib.call("oscar_sst_weights_per_head", key.data_ptr(), n, h, key.stride(0), key.stride(1), c.data_ptr(),
               weights.data_ptr(), totals.data_ptr(), _stream(key))
     return weights

@@ -113,7 +113,11 @@ class CalibrationSession:
         else:
             k = key[:take].reshape(take, h, DIM)
             v = value[:take].reshape(take, h, DIM)
-            w = self.ops.sst_weights_per_head(k, state["q_cov"], state["weight_sum"])
+            prepared = state.get("q_cov_sst")
+            if prepared is None:
+                w = self.ops.sst_weights_per_head(k, state["q_cov"], state["weight_sum"])
+            else:
+                w = self.ops.sst_weights_per_head(k, state["q_cov"], state["weight_sum"], prepared=prepared)
             self.ops.accumulate_gram_grouped(v, state["v_sum"], w)
         state[counter] += take
 
@@ -137,8 +141,13 @@ class CalibrationSession:
         totals = {i: self.states[i]["q_tokens_total"] for i in layers}
         if not totals or min(totals.values()) < DIM:
             raise RuntimeError(f"Insufficient real-model Q samples; no rotations generated: {totals}")
+        # operators that keep a prepared form of the query covariances (the tensor-core
+        # SST kernel's exact bf16 split) build it here, once for the whole second pass
+        prepare = getattr(self.ops, "prepare_sst_covariances", None)
         for state in self.states.values():
             state["q_cov"] = self.ops.normalize(state["q_sum"], state["q_tokens_total"] * self.group_size)
+            if prepare is not None:
+                state["q_cov_sst"] = prepare(state["q_cov"])
         self.phase = 2
         return {"phase": 2, "tokens_per_layer": {i: s["q_tokens"] for i, s in self.states.items()}}
 

@@ -81,6 +81,13 @@ def test_sst_weights_reject_keys_that_are_not_16_byte_rows():
         assert fn(ok_ptr, 1, 1, 260, 256, ok_ptr, ok_ptr, ok_ptr, None) == 1
         assert fn(ok_ptr, 1, 1, 256, 260, ok_ptr, ok_ptr, ok_ptr, None) == 1
         assert fn(ok_ptr, 0, 1, 260, 260, ok_ptr, ok_ptr, ok_ptr, None) == 0  # nothing to do
+    split = handle.oscar_sst_weights_split  # pre-split covariances, nullable status word
+    assert split(off_ptr, 1, 1, 256, 256, ok_ptr, ok_ptr, ok_ptr, None, None) == 1
+    assert split(ok_ptr, 1, 1, 260, 256, ok_ptr, ok_ptr, ok_ptr, None, None) == 1
+    assert split(ok_ptr, 1, 0, 256, 256, ok_ptr, ok_ptr, ok_ptr, None, None) == 1
+    assert split(ok_ptr, 0, 1, 260, 260, ok_ptr, ok_ptr, ok_ptr, None, None) == 0
+    assert handle.oscar_split_bf16x3(ok_ptr, -1, ok_ptr, None) == 1
+    assert handle.oscar_split_bf16x3(ok_ptr, 1, off_ptr, None) == 1
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):

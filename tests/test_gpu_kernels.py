@@ -14,6 +14,7 @@ import torch
 
 from oracle import calibration_oracle as co
 from oracle import int2_oracle as oo
+from oscar_new_b200 import _lib
 from oscar_new_b200 import calibration_kernels as ck
 from oscar_new_b200 import kernels
 from oscar_new_b200.config import OscarConfig, task_capacity
@@ -671,6 +672,41 @@ def test_sst_weights_match_fp64(cuda_lib):
     expect1 = torch.einsum("nhi,ij,nhj->nh", kd, covs[1].double(), kd).clamp_min(0).reshape(-1)
     torch.testing.assert_close(w1.cpu().double(), expect1, rtol=1e-5, atol=1e-6 * float(expect1.max()))
     torch.testing.assert_close(total.cpu().double(), expect1.sum(), rtol=1e-5, atol=0.0)
+
+
+@pytest.mark.parametrize("n,strided", [(300, True), (1024, False)])
+def test_sst_weights_tcgen05_from_split_covariances(cuda_lib, n, strided):
+    """The exact three-part bf16 split of the covariances, and the tcgen05 SST kernel
+    fed by it (called through the C ABI, so a fallback cannot hide) against fp64: 300
+    rows (not a multiple of the 128-row tile) of a strided key view, and the config-5
+    call shape (1024 tokens x 4 KV heads)."""
+    torch.manual_seed(37 + n)
+    h = 4
+    k = torch.randn(n, 2 * h, 256).bfloat16()[:, ::2] if strided else torch.randn(n, h, 256).bfloat16()
+    x = torch.randn(h, 700, 256)
+    x[..., :8] = 20 * torch.distributions.StudentT(3.0).sample((h, 700, 8))
+    covs = (x.transpose(-1, -2) @ x / 700).to(DEV)
+    parts = ck.prepare_sst_covariances(covs)
+    assert torch.equal(parts.double().sum(1), covs.double())  # hi + mid + lo == C exactly
+    kd = k.double()
+    expect = torch.einsum("nhi,hij,nhj->nh", kd, covs.cpu().double(), kd).clamp_min(0)
+    kdev = k.to(DEV)
+    totals = torch.zeros(h, device=DEV)
+    w = torch.empty(n * h, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    rc = _lib.lib().oscar_sst_weights_split(kdev.data_ptr(), n, h, kdev.stride(0), kdev.stride(1), parts.data_ptr(),
+                                            w.data_ptr(), totals.data_ptr(), status.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    scale = float(expect.abs().max())
+    torch.testing.assert_close(w.cpu().double().view(n, h), expect, rtol=1e-5, atol=1e-6 * scale)
+    torch.testing.assert_close(totals.cpu().double(), expect.sum(0), rtol=1e-5, atol=0.0)
+    # the wrapper takes the same path when given the prepared parts
+    totals2 = torch.zeros(h, device=DEV)
+    w2 = ck.sst_weights_per_head(kdev, covs, totals2, prepared=parts)
+    assert torch.equal(w2, w)
 
 
 def test_device_eigensolver_reconstructs_and_matches_eigvalsh(cuda_lib):
