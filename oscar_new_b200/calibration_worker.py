@@ -30,6 +30,7 @@ from __future__ import annotations
 import functools
 import os
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import torch
@@ -197,11 +198,12 @@ class CalibrationSession:
         gram = torch.matmul(rotations.transpose(-1, -2), rotations)
         eye = torch.eye(DIM, dtype=rotations.dtype, device=rotations.device)
         valid = (torch.isfinite(rotations).flatten(1).all(1)
-                 & ((gram - eye).abs() <= 0.005 + 0.005 * eye).flatten(1).all(1)).cpu()
-        rotations_cpu, eigenvalues_cpu = rotations.cpu(), eigenvalues.cpu()
+                 & ((gram - eye).abs() <= 0.005 + 0.005 * eye).flatten(1).all(1))
+        rotations_cpu, eigenvalues_cpu, valid = _to_host(rotations, eigenvalues, valid)
         output = Path(output_dir)
         output.mkdir(parents=True, exist_ok=True)
         layers = sorted(self.states)
+        files = []
         for kind, offset, objective in (("k", 0, "qqt_r_h_pbr"), ("v", 1, "sst_r_h_pbr")):
             result = {
                 "format_version": 1,
@@ -219,16 +221,36 @@ class CalibrationSession:
                 "layers": {},
             }
             for number, index in enumerate(layers):
-                matrix = rotations_cpu[number * 2 + offset]
+                # a copy of its own: a view would make the file carry the whole K + V stack
+                matrix = rotations_cpu[number * 2 + offset].clone()
                 if not bool(valid[number * 2 + offset]):
                     raise RuntimeError(f"Generated {kind} rotation for layer {index} failed validation")
                 result["layers"][index] = {"layer_id": index, "rotation": matrix,
-                                           "eigenvalues": eigenvalues_cpu[number * 2 + offset]}
-            path = output / f"{kind}_rotation.pt"
-            temporary = path.with_suffix(".pt.tmp")
-            torch.save(result, temporary)
-            os.replace(temporary, path)
+                                           "eigenvalues": eigenvalues_cpu[number * 2 + offset].clone()}
+            files.append((result, output / f"{kind}_rotation.pt"))
+        # both files are validated; write them side by side (serialisation and the zip
+        # checksums release the interpreter lock) and publish each by an atomic rename
+        with ThreadPoolExecutor(max_workers=len(files)) as pool:
+            for done in [pool.submit(_publish, result, path) for result, path in files]:
+                done.result()
         return {"rank": 0, "published": True, **convergence}
+
+
+def _to_host(*tensors):
+    """Device tensors to host copies through pinned buffers, one synchronisation."""
+    if not tensors[0].is_cuda:
+        return tuple(t.cpu() for t in tensors)
+    host = tuple(torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in tensors)
+    for h, t in zip(host, tensors):
+        h.copy_(t, non_blocking=True)
+    torch.cuda.current_stream(tensors[0].device).synchronize()
+    return host
+
+
+def _publish(result, path):
+    temporary = path.with_suffix(".pt.tmp")
+    torch.save(result, temporary)
+    os.replace(temporary, path)
 
 
 # --- vLLM worker extension (reference calibration_worker.py:14-50) --------------------

@@ -153,6 +153,8 @@ def test_finish_publishes_loadable_checkpoints(tmp_path):
         ck = torch.load(tmp_path / f"{kind}_rotation.pt", weights_only=True)
         assert ck["format_version"] == 1 and ck["source_grouping"] == "layer"
         assert sorted(ck["layers"]) == [2, 3] and ck["calibration"]["tokens_per_layer"] == {2: 300, 3: 300}
+        # every matrix is stored on its own, not as a view of the K + V stack
+        assert all(e["rotation"].untyped_storage().nbytes() == D * D * 4 for e in ck["layers"].values())
         r = get_rotation(str(tmp_path / f"{kind}_rotation.pt"), "model.layers.3.self_attn.attn", "cpu")
         assert r.dtype == torch.bfloat16 and r.shape == (D, D)
     assert not list(tmp_path.glob("*.tmp"))
