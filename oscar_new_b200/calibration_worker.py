@@ -168,12 +168,12 @@ class CalibrationSession:
         # startup-only scalar check; no activations leave the device
         if not bool(torch.isfinite(weights).all()) or not bool((weights > 0).all()):
             raise RuntimeError("Degenerate SST weights")
-        matrices = []
-        for j, i in enumerate(layers):
-            q = self.states[i]["q_cov"].sum(0)
-            v = sum(self.ops.normalize(vsum[j, h], weights[j, h : h + 1]) for h in range(self.heads))
-            matrices.extend((q, v))
-        stack = torch.stack(matrices)
+        # per layer: Cq = sum over KV heads of the normalised query Grams, Cv = sum over
+        # KV heads of v_sum / max(weight_sum, 1e-30); all layers at once, stacked as
+        # [Cq_0, Cv_0, Cq_1, Cv_1, ...]
+        q = torch.stack([self.states[i]["q_cov"] for i in layers]).sum(1)
+        v = (vsum / weights.clamp_min(1e-30)[:, :, None, None]).sum(1)
+        stack = torch.stack((q, v), 1).reshape(2 * len(layers), DIM, DIM)
         world, _ = self._world()
         if self.shard == "heads":
             self._all_reduce(stack)
