@@ -37,7 +37,7 @@ constexpr int kMtpThreads = 128 * kMtpHeadsPerCta;
 // per-head shared-memory block (bytes)
 template <int NT>
 struct MtpLayout {
-  static constexpr int qfrag = 0;                       // [NT][16 k-steps][32 lanes] uint2
+  static constexpr int qfrag = 0;                       // [NT][8 k-step pairs][32 lanes] uint4
   static constexpr int qm = qfrag + NT * 16 * 32 * 8;   // [NT * 8] row scales
   static constexpr int xmax = qm + 32 * 4;              // [NT][4 t][2 r][4 warps] chunk row maxima
   static constexpr int pbuf = xmax + 4 * NT * 8 * 4;    // [4 k-steps][NT][32 lanes] uint2 P' fragments
@@ -154,7 +154,8 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
   };
 
   // ---- query fragments of the head: warp w < NT computes n-tile w ----
-  uint2 *qfrag = reinterpret_cast<uint2 *>(hs + L::qfrag);
+  // k-steps 2m and 2m + 1 of a lane side by side: one 16-byte load feeds two MMAs
+  uint4 *qfrag = reinterpret_cast<uint4 *>(hs + L::qfrag);
   float *qm_row = reinterpret_cast<float *>(hs + L::qm);
   if (w < NT && nchunks > 0) {
     const int r_mine = 8 * w + gi;
@@ -164,7 +165,8 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
     QueryFrags Q;
     load_query_frags(Q, P.query + (int64_t)qtok * P.qs0 + (int64_t)qhead * P.qs1, rvalid, P.scale_log2);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) qfrag[(w * 16 + k) * 32 + lane] = make_uint2(Q.qf[k][0], Q.qf[k][1]);
+    for (int m = 0; m < 8; ++m)
+      qfrag[(w * 8 + m) * 32 + lane] = make_uint4(Q.qf[2 * m][0], Q.qf[2 * m][1], Q.qf[2 * m + 1][0], Q.qf[2 * m + 1][1]);
     if (gi == 0) {
       qm_row[8 * w + 2 * t] = Q.qm[0];
       qm_row[8 * w + 2 * t + 1] = Q.qm[1];
@@ -245,8 +247,13 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
       for (int n = 0; n < NT; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
 #pragma unroll
       for (int wd = 0; wd < 4; ++wd) {
+        uint4 qp[NT];  // query fragments of k-steps 4 wd + p, p of one pair
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
+          if ((p & 1) == 0) {
+#pragma unroll
+            for (int n = 0; n < NT; ++n) qp[n] = qfrag[(n * 8 + 2 * wd + (p >> 1)) * 32 + lane];
+          }
           const uint32_t xa = (kaw[wd] >> (2 * p)) & 0x03030303u;
           const uint32_t xb = (kbw[wd] >> (2 * p)) & 0x03030303u;
           const uint32_t sa = xa * 0x11u + 0x40404040u, sb = xb * 0x11u + 0x40404040u;
@@ -256,8 +263,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) history_mtp_kernel(HistParams 
           const uint32_t a3 = prmt(lB.lo, lB.hi, sb >> 16);
 #pragma unroll
           for (int n = 0; n < NT; ++n) {
-            const uint2 q = qfrag[(n * 16 + 4 * wd + p) * 32 + lane];
-            mma_f16_16816(sc[n], a0, a1, a2, a3, q.x, q.y);
+            mma_f16_16816(sc[n], a0, a1, a2, a3, (p & 1) ? qp[n].z : qp[n].x, (p & 1) ? qp[n].w : qp[n].y);
           }
         }
       }
