@@ -34,10 +34,11 @@ namespace oscar {
 // The per-half sums of the bisection share one warp reduction (the upper half's count
 // is carried in the high 16 bits); min / max reductions stay inside each half.
 // ----------------------------------------------------------------------------
-OSCAR_DEVINL uint32_t half_sum(uint32_t c) {
-  const bool upper = (threadIdx.x & 16) != 0;
-  const uint32_t total = __reduce_add_sync(0xffffffffu, upper ? (c << 16) : c);
-  return upper ? (total >> 16) : (total & 0xffffu);
+// sh = 16 on the upper half's lanes, 0 on the lower half's (half_shift()).
+OSCAR_DEVINL uint32_t half_shift() { return (threadIdx.x & 16u); }
+OSCAR_DEVINL uint32_t half_sum(uint32_t c, uint32_t sh) {
+  const uint32_t total = __reduce_add_sync(0xffffffffu, c << sh);
+  return (total >> sh) & 0xffffu;
 }
 
 OSCAR_DEVINL float half_max(float v) {
@@ -91,12 +92,13 @@ OSCAR_DEVINL uint32_t half_kth_largest_bf16(const uint32_t (&mag)[8], int k, uin
   m2 = __hmax2(m2, __hmax2(__hmax2(as_bf2(mag[4]), as_bf2(mag[5])), __hmax2(as_bf2(mag[6]), as_bf2(mag[7]))));
   const uint32_t mb = bf2_bits(m2);
   const int e = (int)(half_umax(max(mb & 0xffffu, mb >> 16)) >> 7);
+  const uint32_t sh = half_shift();
   bool found = false;
   uint32_t v = 0, cv = 256;
 #pragma unroll 1
   for (int p = 0; p < 4; ++p) {
     const uint32_t t = (uint32_t)max(e - p, 0) << 7;
-    const uint32_t c = half_sum(count_ge_bf16(mag, t));
+    const uint32_t c = half_sum(count_ge_bf16(mag, t), sh);
     if (!found && c >= (uint32_t)k) {
       found = true;
       v = t;
@@ -104,13 +106,27 @@ OSCAR_DEVINL uint32_t half_kth_largest_bf16(const uint32_t (&mag)[8], int k, uin
     }
     if (__all_sync(0xffffffffu, found)) break;
   }
+  if (__all_sync(0xffffffffu, found)) {
+    // the usual case: both halves know their binade; the 7 mantissa bits, unrolled
+#pragma unroll
+    for (int b = 6; b >= 0; --b) {
+      const uint32_t t = v | (1u << b);
+      const uint32_t c = half_sum(count_ge_bf16(mag, t), sh);
+      if (c >= (uint32_t)k) {
+        v = t;
+        cv = c;
+      }
+    }
+    *count = cv;
+    return v;
+  }
   const int nb = found ? 7 : 15;
   const int steps = __reduce_max_sync(0xffffffffu, (unsigned)nb);
 #pragma unroll 1
   for (int s = 0; s < steps; ++s) {
     const int b = nb - 1 - s;
     const uint32_t t = b >= 0 ? (v | (1u << b)) : 0x7fffu;  // 0x7fff: counts nothing
-    const uint32_t c = half_sum(count_ge_bf16(mag, t));
+    const uint32_t c = half_sum(count_ge_bf16(mag, t), sh);
     if (c >= (uint32_t)k && b >= 0) {
       v = t;
       cv = c;
