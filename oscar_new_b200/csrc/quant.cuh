@@ -289,8 +289,10 @@ OSCAR_DEVINL void quantize_pack_half(const uint32_t (&w)[8], const oscar_clip &c
   for (int i = 0; i < 8; ++i) {
     const __nv_bfloat162 x = as_bf2(w[i]);
     const uint32_t m1 = __hge2_mask(x, B1), m2 = __hge2_mask(x, B2), m3 = __hge2_mask(x, B3);
-    const uint32_t r = ((m1 ^ m2 ^ m3) & 0x00010001u) | (m2 & 0x00020002u);
-    u[i >> 2] |= r << (4 * (i & 3));
+    // the masks are all-ones or all-zeros per half, so the code bits go straight to
+    // their packed position: bit 0 (m1 ^ m2 ^ m3) and bit 1 (m2) of element pair i
+    const uint32_t lo_bit = 0x00010001u << (4 * (i & 3)), hi_bit = 0x00020002u << (4 * (i & 3));
+    u[i >> 2] |= ((m1 ^ m2 ^ m3) & lo_bit) | (m2 & hi_bit);
   }
   // element 2i at bit 4i, element 2i+1 at bit 16 + 4i -> 4i + 2
   const uint32_t packed = ((u[0] | (u[0] >> 14)) & 0xffffu) | (((u[1] | (u[1] >> 14)) & 0xffffu) << 16);
