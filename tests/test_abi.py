@@ -154,3 +154,17 @@ def test_binding_argument_types_follow_the_header_prototypes():
         for i, (g, w) in enumerate(zip(got, want)):
             assert g is w, (name, i, g, w)
         assert _lib._RESTYPES.get(name, ctypes.c_int) is (ctypes.c_int64 if ret == "int64_t" else ctypes.c_int), name
+
+
+def test_sst_preparation_refuses_host_tensors_and_foreign_parts():
+    """The tensor-core SST path is device-only, and its prepared covariances must be the
+    [h, 3, 256, 256] bf16 split of the same covariances (checked before any launch)."""
+    import torch
+
+    from oscar_new_b200 import calibration_kernels as ck
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ck.prepare_sst_covariances(torch.zeros(2, 256, 256))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ck.sst_weights_per_head(torch.zeros(4, 2, 256, dtype=torch.bfloat16), torch.zeros(2, 256, 256),
+                                torch.zeros(2), prepared=torch.zeros(2, 3, 256, 256, dtype=torch.bfloat16))
