@@ -164,6 +164,8 @@ def calibrated_rotations(covariances: torch.Tensor, max_sweeps: int = 12, tolera
     status = host[:, 2]
     residual = float(host[:, 1].max())
     result = {"sweeps": int(host[:, 0].max()), "relative_off_diagonal": residual}
+    if bool((status == 3).any()):
+        raise RuntimeError("calibration eigensolver: a device wait timed out; rotations not published")
     if bool((status == 2).any()):
         raise RuntimeError("non-finite calibration covariance; rotations not published")
     if not residual < tolerance:

@@ -4,10 +4,10 @@
 //
 // Eigensolver: the parallel cyclic (round-robin) Jacobi of the reference, with all
 // sweeps inside one launch.  A thread-block cluster of 8 CTAs owns one 256x256
-// matrix; CTA r holds rows [32r, 32r+32) of A and of U in shared memory (the column
-// rotations are row-local), and the row rotations exchange partner rows through
-// distributed shared memory.  Cluster barriers are hardware barriers (no software
-// spin), and the sweep count is bounded.
+// matrix; CTA r holds rows [32r, 32r+32) of W = C V and of V in registers (the column
+// rotations are row-local), and the three dot products that define each rotation are
+// summed across the cluster through distributed shared memory.  Cluster barriers are
+// hardware barriers (no software spin), and the sweep count is bounded.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -271,18 +271,63 @@ __global__ void normalize_kernel(const float *__restrict__ x, int64_t numel, con
 // ----------------------------------------------------------------------------
 constexpr int kJCtas = 8;
 constexpr int kJRows = kDim / kJCtas;  // 32 rows per CTA
-constexpr int kJThreads = 512;  // 16 warps: a round is latency-bound (remote rows, barriers)
+constexpr int kJGroups = kDim / 4;  // groups of two pairs of a round
+constexpr int kJThreads = 4 * kJGroups;  // 8 warps: 4 lanes (8 rows each) per group
 constexpr int kJWarps = kJThreads / 32;
+constexpr int kJLaneRows = kJRows / 4;  // rows per lane
+constexpr int kJPairStride = 4 * kJCtas + 2;  // doubles per pair in JacobiSmem::all
 
 struct JacobiSmem {
-  double a[kJRows][kDim];  // local rows of W = C V (columns rotated every round); epilogue scratch
-  double u[kJRows][kDim];  // local rows of V (the accumulated rotations)
-  double cs[kDim / 2][2];
-  double part4[4][kDim / 2][3];           // per row group: a_pp, a_qq, a_pq of each pair
-  double all[2][kJCtas][kDim / 2][3];     // every CTA's sums, pushed here; double-buffered by round
+  double a[kJRows][kDim];  // local rows of W = C V at the start and the end; epilogue scratch
+  double u[kJRows][kDim];  // local rows of V (the accumulated rotations), likewise
+  // every CTA's a_pp, a_qq, a_pq of each pair, pushed here (group m, pair k, CTA c at
+  // [m][k * kJPairStride + 4c]); double-buffered by round.  The 560-byte group stride
+  // keeps the 16-byte reads of a quarter warp (two groups x four lanes) on distinct banks.
+  double all[2][kJGroups][2 * kJPairStride + 2];
+  // (W, V) rows of the q columns leaving a warp's last group and of the p columns leaving
+  // its first group, lane-interleaved: four lanes store 64 contiguous bytes per row
+  double2 edge_q[kJWarps][kJLaneRows][4];
+  double2 edge_p[kJWarps][kJLaneRows][4];
   double diag[kDim];
   double evpart[kDim];                    // this CTA's share of the Rayleigh quotients
+  uint64_t xbar[2];                       // completes when all[b] holds every CTA's sums
+  int32_t abort;                          // a wait for the sums gave up
 };
+constexpr uint32_t kJXBytes = kJCtas * kJGroups * 2 * 24;  // bytes pushed into a CTA per round
+
+// shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster
+OSCAR_DEVINL uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+// stores into another CTA's shared memory that complete their bytes on its mbarrier
+OSCAR_DEVINL void st_async_f64x2(uint32_t addr, double a, double b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f64 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "d"(a), "d"(b), "r"(bar)
+               : "memory");
+}
+OSCAR_DEVINL void st_async_f64(uint32_t addr, double a, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f64 [%0], %1, [%2];" ::"r"(addr), "d"(a),
+               "r"(bar)
+               : "memory");
+}
+
+// bounded wait for a phase whose bytes other CTAs of the cluster wrote
+OSCAR_DEVINL bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t phase) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 "
+        "%0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
 
 // x mod (D-1) for x in (-(D-1), 2(D-1)): two conditional corrections, no division.
 OSCAR_DEVINL int mod_dm1(int x) {
@@ -307,10 +352,19 @@ OSCAR_DEVINL void round_pair(int j, int r, int &p, int &q) {
 // a_pq = v_p . w_q, the entries of the implicit A; its formula, skip rule and
 // convergence test (max|a_pq| / max|a_pp| of a sweep) are the reference's.  Column
 // updates are row-local, so a round needs only the cluster sums of the three dot
-// products (each CTA's sums over its 32 rows, read over distributed shared memory) and
-// ONE cluster barrier, where the row-rotating form exchanged partner rows with two.
-// The eigenvalues are the Rayleigh quotients v_p . w_p.  fp64 arithmetic (the
-// reference uses fp32).
+// products (each CTA's sums over its 32 rows, pushed into every CTA over distributed
+// shared memory) and ONE cluster barrier, where the row-rotating form exchanged partner
+// rows with two.  The eigenvalues are the Rayleigh quotients v_p . w_p.  fp64
+// arithmetic (the reference uses fp32).
+//
+// The columns live in registers.  Round r pairs seat k with seat 255 - k (pair k,
+// k = 1..127; pair 0 = seat 0 with column 255), and column x sits at seat x - r mod 255:
+// from one round to the next every column moves one seat down the ring.  Pairs 2m and
+// 2m + 1 (group m) are held by lanes 4(m % 8) .. 4(m % 8) + 3 of warp m / 8, lane g of
+// them holding rows 8g .. 8g + 7 of the four columns of W and V.  Half of the moves stay
+// inside a group (register copies); the other half are a shuffle by 4 lanes, with the
+// columns that cross a warp boundary staged in shared memory, so a round reads no
+// matrix data from shared memory.
 OSCAR_DEVINL double rsqrt_f64(double x) {
   // fp32 seed, two Newton steps: about 46 bits, then the fp64 rounding
   double y = (double)rsqrtf((float)x);
@@ -340,96 +394,175 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float *C = cov + (size_t)batch * kDim * kDim;
   const int row0 = rank * kJRows;
+  if (tid == 0) {
+    mbar_init(&S.xbar[0], 1);
+    mbar_init(&S.xbar[1], 1);
+    S.abort = 0;
+    fence_mbarrier_init();
+  }
   for (int e = tid; e < kJRows * kDim; e += kJThreads) {
     const int r = e / kDim, c = e % kDim;
     const int gr = row0 + r;
     S.a[r][c] = ((double)C[gr * kDim + c] + (double)C[c * kDim + gr]) * 0.5;
     S.u[r][c] = gr == c ? 1.0 : 0.0;
   }
-  __syncthreads();
+  cluster.sync();  // every CTA's barriers are initialised before the first push
+  // this lane's two pairs (seats of round 0) and rows
+  const int m = tid >> 2, g = tid & 3;
+  double wp[2][kJLaneRows], wq[2][kJLaneRows], vp[2][kJLaneRows], vq[2][kJLaneRows];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    int p, q;
+    round_pair(2 * m + k, 0, p, q);
+#pragma unroll
+    for (int i = 0; i < kJLaneRows; ++i) {
+      const int lr = g * kJLaneRows + i;
+      wp[k][i] = S.a[lr][p], wq[k][i] = S.a[lr][q], vp[k][i] = S.u[lr][p], vq[k][i] = S.u[lr][q];
+    }
+  }
   double residual = INFINITY;
   int sweeps_done = 0;
-  bool finite = true;
-  int buf = 0;
-  for (int sweep = 0; sweep < max_sweeps; ++sweep) {
+  bool finite = true, timed_out = false;
+  uint32_t round_no = 0;  // rounds so far: buffer round_no & 1, its phase (round_no >> 1) & 1
+  for (int sweep = 0; sweep < max_sweeps && !timed_out; ++sweep) {
     double smax = 0.0, dmax = 0.0;  // largest |a_pq| and |a_pp| seen in this sweep
     bool sfin = true;
-    for (int r = 0; r < kDim - 1; ++r) {
-      // (1) this CTA's a_pp, a_qq, a_pq of every pair of the round, over its 32 rows
+#pragma unroll 1
+    for (int r = 0; r < kDim - 1; ++r, ++round_no) {
+      const int buf = (int)(round_no & 1u);
+      if (tid == 0) mbar_arrive_expect_tx(&S.xbar[buf], kJXBytes);
+      // (1) this CTA's a_pp, a_qq, a_pq of the lane's pairs over its 32 rows (each lane
+      // 8 rows, then (g0 + g1) + (g2 + g3)); lane g pushes them into CTAs g, g + 4, whose
+      // barrier for this buffer counts the bytes.  A CTA writes buffer b of round n + 2
+      // only after every CTA's sums of round n + 1 reached it, and each CTA pushes those
+      // after it has read its sums of round n, so double buffering needs no barrier.
       {
-        const int j = tid & (kDim / 2 - 1), rg = tid >> 7;
-        int p, q;
-        round_pair(j, r, p, q);
-        double app = 0.0, aqq = 0.0, apq = 0.0;
+        double app[2] = {0.0, 0.0}, aqq[2] = {0.0, 0.0}, apq[2] = {0.0, 0.0};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int lr = rg * 8 + i;
-          const double vp = S.u[lr][p], vq = S.u[lr][q], wp = S.a[lr][p], wq = S.a[lr][q];
-          app = fma(vp, wp, app);
-          aqq = fma(vq, wq, aqq);
-          apq = fma(vp, wq, apq);
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+          for (int i = 0; i < kJLaneRows; ++i) {
+            app[k] = fma(vp[k][i], wp[k][i], app[k]);
+            aqq[k] = fma(vq[k][i], wq[k][i], aqq[k]);
+            apq[k] = fma(vp[k][i], wq[k][i], apq[k]);
+          }
+#pragma unroll
+        for (int s = 1; s <= 2; s <<= 1)
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            app[k] += __shfl_xor_sync(0xffffffffu, app[k], s);
+            aqq[k] += __shfl_xor_sync(0xffffffffu, aqq[k], s);
+            apq[k] += __shfl_xor_sync(0xffffffffu, apq[k], s);
+          }
+#pragma unroll
+        for (int c = g; c < kJCtas; c += 4) {
+          const uint32_t dst = cluster_addr(S.all[buf][m] + 4 * rank, (uint32_t)c);
+          const uint32_t bar = cluster_addr(&S.xbar[buf], (uint32_t)c);
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            st_async_f64x2(dst + 8u * (uint32_t)(k * kJPairStride), app[k], aqq[k], bar);
+            st_async_f64(dst + 8u * (uint32_t)(k * kJPairStride + 2), apq[k], bar);
+          }
         }
-        S.part4[rg][j][0] = app;
-        S.part4[rg][j][1] = aqq;
-        S.part4[rg][j][2] = apq;
       }
-      __syncthreads();
-      // push this CTA's sums into every CTA of the cluster (stores do not stall; the
-      // cluster barrier makes them visible), so step 2 reads only local shared memory
-      if (tid < 3 * (kDim / 2)) {
-        const int j = tid / 3, k = tid % 3;
-        const double v = (S.part4[0][j][k] + S.part4[1][j][k]) + (S.part4[2][j][k] + S.part4[3][j][k]);
-#pragma unroll
-        for (int c = 0; c < kJCtas; ++c) cluster.map_shared_rank(&S, c)->all[buf][rank][j][k] = v;
-      }
-      cluster.sync();
-      // (2) cluster sums and the rotation of each pair, four lanes per pair: lane c2 adds
-      // CTAs 2 c2 and 2 c2 + 1, a fixed shuffle tree adds the rest (the same order in
-      // every CTA, so every CTA derives the same rotations)
+      if (!mbar_wait_cluster_bounded(&S.xbar[buf], (round_no >> 1) & 1u)) S.abort = 1;
+      // (2) cluster sums and the rotation of each pair: lane g adds CTAs g and g + 4, a
+      // fixed shuffle tree adds the rest (the same order in every CTA, so every CTA and
+      // every lane of the group derives the same rotations)
+      double cs[2], sn[2];
       {
-        const int j = tid >> 2, c2 = tid & 3;
-        const double *x0 = S.all[buf][2 * c2][j], *x1 = S.all[buf][2 * c2 + 1][j];
-        double app = x0[0] + x1[0];
-        double aqq = x0[1] + x1[1];
-        double apq = x0[2] + x1[2];
+        double app[2], aqq[2], apq[2];
 #pragma unroll
-        for (int m = 1; m <= 2; m <<= 1) {
-          app += __shfl_xor_sync(0xffffffffu, app, m);
-          aqq += __shfl_xor_sync(0xffffffffu, aqq, m);
-          apq += __shfl_xor_sync(0xffffffffu, apq, m);
+        for (int k = 0; k < 2; ++k) {
+          const double2 *x = reinterpret_cast<const double2 *>(S.all[buf][m] + k * kJPairStride + 4 * g);
+          const double2 a01 = x[0], a2_ = x[1], b01 = x[8], b2_ = x[9];
+          app[k] = a01.x + b01.x;
+          aqq[k] = a01.y + b01.y;
+          apq[k] = a2_.x + b2_.x;
         }
-        if (!isfinite(app) || !isfinite(aqq) || !isfinite(apq)) sfin = false;
-        smax = fmax(smax, fabs(apq));
-        dmax = fmax(dmax, fmax(fabs(app), fabs(aqq)));
-        const double delta = (aqq - app) * 0.5;
-        const double sgn = delta >= 0.0 ? 1.0 : -1.0;
-        const double h2 = fma(delta, delta, apq * apq);
-        const double h = h2 > 0.0 ? h2 * rsqrt_f64(h2) : 0.0;
-        double tang = sgn * apq * rcp_f64(fmax(fabs(delta) + h, 1e-300));
-        if (!(fabs(apq) > 1e-8 * (fabs(app) + fabs(aqq)) + 1e-20)) tang = 0.0;
-        const double cs = rsqrt_f64(fma(tang, tang, 1.0));
-        if (c2 == 0) {
-          S.cs[j][0] = cs;
-          S.cs[j][1] = tang * cs;
+#pragma unroll
+        for (int s = 1; s <= 2; s <<= 1)
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            app[k] += __shfl_xor_sync(0xffffffffu, app[k], s);
+            aqq[k] += __shfl_xor_sync(0xffffffffu, aqq[k], s);
+            apq[k] += __shfl_xor_sync(0xffffffffu, apq[k], s);
+          }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (!isfinite(app[k]) || !isfinite(aqq[k]) || !isfinite(apq[k])) sfin = false;
+          smax = fmax(smax, fabs(apq[k]));
+          dmax = fmax(dmax, fmax(fabs(app[k]), fabs(aqq[k])));
+          const double delta = (aqq[k] - app[k]) * 0.5;
+          const double sgn = delta >= 0.0 ? 1.0 : -1.0;
+          const double h2 = fma(delta, delta, apq[k] * apq[k]);
+          const double h = h2 > 0.0 ? h2 * rsqrt_f64(h2) : 0.0;
+          double tang = sgn * apq[k] * rcp_f64(fmax(fabs(delta) + h, 1e-300));
+          if (!(fabs(apq[k]) > 1e-8 * (fabs(app[k]) + fabs(aqq[k])) + 1e-20)) tang = 0.0;
+          cs[k] = rsqrt_f64(fma(tang, tang, 1.0));
+          sn[k] = tang * cs[k];
         }
       }
-      __syncthreads();
-      // (3) rotate columns p, q of the local rows of W and V
-      for (int e = tid; e < kJRows * (kDim / 2); e += kJThreads) {
-        const int lr = e / (kDim / 2), j = e % (kDim / 2);
-        int p, q;
-        round_pair(j, r, p, q);
-        const double c = S.cs[j][0], s = S.cs[j][1];
-        const double wp = S.a[lr][p], wq = S.a[lr][q];
-        S.a[lr][p] = wp * c - wq * s;
-        S.a[lr][q] = wp * s + wq * c;
-        const double up = S.u[lr][p], uq = S.u[lr][q];
-        S.u[lr][p] = up * c - uq * s;
-        S.u[lr][q] = up * s + uq * c;
+      // (3) rotate columns p, q of the lane's rows of W and V
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int i = 0; i < kJLaneRows; ++i) {
+          const double w0 = wp[k][i], w1 = wq[k][i], u0 = vp[k][i], u1 = vq[k][i];
+          wp[k][i] = w0 * cs[k] - w1 * sn[k];
+          wq[k][i] = w0 * sn[k] + w1 * cs[k];
+          vp[k][i] = u0 * cs[k] - u1 * sn[k];
+          vq[k][i] = u0 * sn[k] + u1 * cs[k];
+        }
+      // (4) every column one seat down.  Within a group: pair 2m takes pair 2m + 1's p,
+      // pair 2m + 1 takes pair 2m's q.  Across groups: pair 2m takes group m - 1's second
+      // q, pair 2m + 1 group m + 1's first p.  Pair 0 keeps column 255 and takes pair 1's
+      // p as its q; pair 127 turns its q into its p.  Columns crossing a warp boundary go
+      // through shared memory (the previous round's readers are past this round's
+      // cluster barrier).
+      if (lane >= 28) {
+#pragma unroll
+        for (int i = 0; i < kJLaneRows; ++i) S.edge_q[warp][i][g] = make_double2(wq[1][i], vq[1][i]);
+      }
+      if (lane < 4) {
+#pragma unroll
+        for (int i = 0; i < kJLaneRows; ++i) S.edge_p[warp][i][g] = make_double2(wp[0][i], vp[0][i]);
       }
       __syncthreads();
-      buf ^= 1;
+      if (S.abort) {  // CTA-uniform after the barrier: stop the sweeps (others time out too)
+        timed_out = true;
+        break;
+      }
+#pragma unroll
+      for (int i = 0; i < kJLaneRows; ++i) {
+        const double wq_up = __shfl_up_sync(0xffffffffu, wq[1][i], 4);
+        const double vq_up = __shfl_up_sync(0xffffffffu, vq[1][i], 4);
+        const double wp_dn = __shfl_down_sync(0xffffffffu, wp[0][i], 4);
+        const double vp_dn = __shfl_down_sync(0xffffffffu, vp[0][i], 4);
+        double nwq0, nvq0, nwp1, nvp1;
+        if (m == 0) {
+          nwq0 = wp[1][i], nvq0 = vp[1][i];
+        } else if (lane >= 4) {
+          nwq0 = wq_up, nvq0 = vq_up;
+        } else {
+          const double2 e = S.edge_q[warp - 1][i][g];
+          nwq0 = e.x, nvq0 = e.y;
+        }
+        if (m == kJGroups - 1) {
+          nwp1 = wq[1][i], nvp1 = vq[1][i];
+        } else if (lane < 28) {
+          nwp1 = wp_dn, nvp1 = vp_dn;
+        } else {
+          const double2 e = S.edge_p[warp + 1][i][g];
+          nwp1 = e.x, nvp1 = e.y;
+        }
+        if (m != 0) wp[0][i] = wp[1][i], vp[0][i] = vp[1][i];
+        wq[1][i] = wq[0][i], vq[1][i] = vq[0][i];
+        wq[0][i] = nwq0, vq[0][i] = nvq0;
+        wp[1][i] = nwp1, vp[1][i] = nvp1;
+      }
     }
+    if (timed_out) break;
     sweeps_done = sweep + 1;
     // the sweep's residual (identical in every CTA: the same sums in the same order)
 #pragma unroll
@@ -448,6 +581,18 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
     residual = finite ? o / fmax(d, 1e-300) : INFINITY;
     if (!finite || residual < (double)tol) break;
   }
+  // after whole sweeps the columns sit at their round-0 seats again
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    int p, q;
+    round_pair(2 * m + k, 0, p, q);
+#pragma unroll
+    for (int i = 0; i < kJLaneRows; ++i) {
+      const int lr = g * kJLaneRows + i;
+      S.a[lr][p] = wp[k][i], S.a[lr][q] = wq[k][i], S.u[lr][p] = vp[k][i], S.u[lr][q] = vq[k][i];
+    }
+  }
+  __syncthreads();
   // eigenvalues: Rayleigh quotients v_p . w_p, summed over the cluster's rows
   for (int i = tid; i < kDim; i += kJThreads) {
     double acc = 0.0;
@@ -514,7 +659,7 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
     float *inf4 = info + (size_t)batch * 4;
     inf4[0] = (float)sweeps_done;
     inf4[1] = (float)residual;
-    inf4[2] = !finite ? 2.f : (residual < (double)tol ? 0.f : 1.f);
+    inf4[2] = timed_out ? 3.f : (!finite ? 2.f : (residual < (double)tol ? 0.f : 1.f));
     inf4[3] = 0.f;
   }
   cluster.sync();  // keep shared memory alive until every remote read is done
