@@ -9,8 +9,9 @@ arithmetic those kernels rely on, over every case rather than a sample:
     in bf16 and read back from the low 7 bits of 128 + n;
   * the MTP kernel's value byte lanes (history_mtp.cu) split the 256 dims among the four
     warps of a head and extract the codes the reference's unpack assigns to those dims;
-  * the Jacobi round (calibration.cu) pairs each local row with the partner and rotation
-    (j, p-or-q) of the reference's round-robin schedule;
+  * the Jacobi ring (calibration.cu): the register moves between rounds keep every pair
+    on the columns of the reference's round-robin schedule, and the partial-sum reads of
+    a quarter warp fall on distinct shared-memory banks;
   * the rotation epilogue's row -> (token, head) split by multiply-high (rotate.cuh);
   * the window store (attention.cu `window_store_kernel`) visits exactly the reference's
     per-slot latest writers, each slot once.
@@ -120,25 +121,49 @@ def test_mtp_value_byte_lanes_partition_the_dims():
                     assert (x >> (16 + 2 * p)) & 3 == codes[1, d]
 
 
-def mod_dm1(x, d=256):
-    x += (d - 1) if x < 0 else 0
-    return x - (d - 1) if x >= d - 1 else x
+def test_jacobi_ring_moves_follow_the_round_robin_schedule():
+    """jacobi_kernel: group m (lanes 4(m % 8) .. + 3 of warp m // 8) holds pairs 2m and
+    2m + 1.  Between rounds: p0 <- p1 (pair 0 keeps column 255), q0 <- group m - 1's q1
+    (pair 0: its own p1), p1 <- group m + 1's p0 (pair 127: its own q1), q1 <- q0; a
+    move from another group is a shuffle by 4 lanes, or a shared-memory hand-over when
+    the groups sit in different warps."""
+    d, groups = 256, 64
+    pairs = [round_robin_pairs(d, r) for r in range(d - 1)]
+
+    def seat(r):
+        p, q = (t.tolist() for t in pairs[r % (d - 1)])
+        return ([p[2 * m] for m in range(groups)], [q[2 * m] for m in range(groups)],
+                [p[2 * m + 1] for m in range(groups)], [q[2 * m + 1] for m in range(groups)])
+
+    p0, q0, p1, q1 = seat(0)
+    crossings = 0
+    for r in range(3 * (d - 1)):
+        assert (p0, q0, p1, q1) == seat(r), r
+        n = ([None] * groups, [None] * groups, [None] * groups, [None] * groups)
+        for m in range(groups):
+            n[0][m] = p0[m] if m == 0 else p1[m]
+            n[1][m] = p1[m] if m == 0 else q1[m - 1]
+            n[2][m] = q1[m] if m == groups - 1 else p0[m + 1]
+            n[3][m] = q0[m]
+            crossings += (m % 8 == 0 and m > 0) + (m % 8 == 7 and m < groups - 1)
+        p0, q0, p1, q1 = n
+    assert crossings == 3 * (d - 1) * 14  # 7 warp boundaries, both directions
 
 
-def test_jacobi_row_partners_follow_the_round_robin_schedule():
-    d = 256
-    for r in range(d - 1):
-        p, q = (t.tolist() for t in round_robin_pairs(d, r))
-        for x in range(d):
-            if x == d - 1:
-                y, j, isp = r, 0, 1
-            elif x == r:
-                y, j, isp = d - 1, 0, 0
-            else:
-                y = mod_dm1(mod_dm1(2 * r - x))
-                jp = mod_dm1(x - r)
-                j, isp = (jp, 1) if 1 <= jp < d // 2 else (mod_dm1(r - x), 0)
-            assert (p[j], q[j]) == ((x, y) if isp else (y, x)), (r, x)
+def test_jacobi_partial_sum_reads_are_bank_conflict_free():
+    """JacobiSmem::all: group stride 560 B, pair k at 272 k, CTA c at 32 c; lane g of group
+    m reads CTAs g and g + 4 as 16-byte loads.  Each quarter warp (8 lanes: two groups x
+    four lanes) must touch 8 distinct 16-byte bank groups in every load."""
+    group_stride, pair_stride = (2 * 34 + 2) * 8, 34 * 8
+    for k in range(2):
+        for load in (0, 16, 128, 144):  # (a_pp, a_qq), (a_pq, pad) of CTAs g and g + 4
+            for quarter in range(4):
+                lanes = range(8 * quarter, 8 * quarter + 8)
+                addr = [(lane >> 2) * group_stride + k * pair_stride + 32 * (lane & 3) + load for lane in lanes]
+                assert all(a % 16 == 0 for a in addr)
+                assert len({(a % 128) // 16 for a in addr}) == 8, (k, load, quarter)
+    # the bytes a CTA expects per round: 8 CTAs x 64 groups x 2 pairs x (16 + 8) bytes
+    assert 8 * 64 * 2 * 24 == 24576 < (1 << 20)
 
 
 def test_row_to_token_division_by_multiply_high():
