@@ -110,14 +110,16 @@ int oscar_prefill_attention(const void *query, int64_t qs0, int64_t qs1, const v
 #define OSCAR_HISTORY_F8_KERNEL 3
 int oscar_last_history_kernel(void);
 
-/* Test hook for the timeout path of the decode history kernels (no counterpart in the
- * reference): from the next launch on, CTA (0, 0, 0) of every history launch (the default
- * mma.sync kernels and the opt-in tcgen05 kernel) never issues the copy of its chunk / tile
- * `withhold` (-1: none), and every bounded device wait of those launches gives up after
- * `wait_probes` probes (0: the default limit of 2^20).  The copy's consumers then time
- * out: the launch stores OSCAR_ERR_TIMEOUT into its status word, marks the aborted CTA's
- * rows empty (lse -inf), lets its issued copies land and returns.  Process-wide; for
- * tests only. */
+/* Test hook for the timeout path of the decode history kernels and the eigensolver (no
+ * counterpart in the reference): from the next launch on, CTA (0, 0, 0) of every history
+ * launch (the default mma.sync kernels and the opt-in tcgen05 kernel) never issues the
+ * copy of its chunk / tile `withhold` (-1: none), CTA 0 of the first matrix's cluster of
+ * every oscar_jacobi_rotations launch never pushes its partial sums of round `withhold`,
+ * and every bounded device wait of those launches gives up after `wait_probes` probes (0:
+ * the default limit of 2^20).  The consumers then time out: a history launch stores
+ * OSCAR_ERR_TIMEOUT into its status word, marks the aborted CTA's rows empty (lse -inf),
+ * lets its issued copies land and returns; the eigensolver reports info status 3 for that
+ * matrix.  Process-wide; for tests only. */
 int oscar_test_set_wait_fault(int32_t withhold, uint32_t wait_probes);
 
 /* Y[n,h,:] = bf16( bf16(X[n,h,:]) @ bf16(R) ), fp32 accumulation.

@@ -1018,6 +1018,8 @@ static std::atomic<int32_t> g_last_history{0};
 // Test hook state (oscar_test_set_wait_fault), read at every history launch.
 static std::atomic<int32_t> g_withhold{-1};
 static std::atomic<uint32_t> g_wait_probes{kWaitLimit};
+int32_t test_hook_withhold() { return g_withhold.load(); }
+uint32_t test_hook_wait_probes() { return g_wait_probes.load(); }
 
 static int history_launch(HistParams P, int32_t num_tasks, cudaStream_t stream, int priority = 0) {
   P.withhold = g_withhold.load();
@@ -1319,10 +1321,11 @@ extern "C" int oscar_decode_attention(const void *qrot, const void *query, int64
 }
 
 // Test hook, no counterpart in the reference: CTA (0, 0, 0) of every later history launch
-// skips the copy of its chunk / tile `withhold` (-1: none) and every bounded device wait of
-// those launches gives up after `wait_probes` probes (0: the default limit).  The skipped
-// copy's consumers then time out, which exercises the timeout path (status word, -inf
-// rows, clean exit).
+// skips the copy of its chunk / tile `withhold` (-1: none), CTA 0 of the first matrix of
+// every later eigensolver launch skips its partial-sum pushes of round `withhold`, and
+// every bounded device wait of those launches gives up after `wait_probes` probes (0: the
+// default limit).  The skipped copy's consumers then time out, which exercises the
+// timeout path (status word / info status, -inf rows, clean exit).
 extern "C" int oscar_test_set_wait_fault(int32_t withhold, uint32_t wait_probes) {
   g_withhold.store(withhold < 0 ? -1 : withhold);
   g_wait_probes.store(wait_probes == 0 ? kWaitLimit : wait_probes);

@@ -292,6 +292,8 @@ struct JacobiSmem {
   double evpart[kDim];                    // this CTA's share of the Rayleigh quotients
   uint64_t xbar[2];                       // completes when all[b] holds every CTA's sums
   int32_t abort;                          // a wait for the sums gave up
+  int32_t hook_round;                     // test hook: this CTA skips its pushes of this round
+  uint32_t wait_probes;                   // probes of a wait before it gives up
 };
 constexpr uint32_t kJXBytes = kJCtas * kJGroups * 2 * 24;  // bytes pushed into a CTA per round
 
@@ -302,21 +304,26 @@ OSCAR_DEVINL uint32_t cluster_addr(const void *p, uint32_t rank) {
   return out;
 }
 
-// stores into another CTA's shared memory that complete their bytes on its mbarrier
-OSCAR_DEVINL void st_async_f64x2(uint32_t addr, double a, double b, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f64 [%0], {%1, %2}, [%3];" ::"r"(addr),
-               "d"(a), "d"(b), "r"(bar)
-               : "memory");
+// stores into another CTA's shared memory that complete their bytes on its mbarrier;
+// issued only when `on` is non-zero (a predicate, not a branch)
+OSCAR_DEVINL void st_async_f64x2(uint32_t addr, double a, double b, uint32_t bar, uint32_t on) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+      " @p st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f64 [%0], {%1, %2}, [%3];\n}" ::"r"(addr),
+      "d"(a), "d"(b), "r"(bar), "r"(on)
+      : "memory");
 }
-OSCAR_DEVINL void st_async_f64(uint32_t addr, double a, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f64 [%0], %1, [%2];" ::"r"(addr), "d"(a),
-               "r"(bar)
-               : "memory");
+OSCAR_DEVINL void st_async_f64(uint32_t addr, double a, uint32_t bar, uint32_t on) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %3, 0;\n"
+      " @p st.async.shared::cluster.mbarrier::complete_tx::bytes.f64 [%0], %1, [%2];\n}" ::"r"(addr),
+      "d"(a), "r"(bar), "r"(on)
+      : "memory");
 }
 
 // bounded wait for a phase whose bytes other CTAs of the cluster wrote
-OSCAR_DEVINL bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t phase) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+OSCAR_DEVINL bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t phase, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 "
@@ -380,9 +387,12 @@ OSCAR_DEVINL double rcp_f64(double x) {
   return y;
 }
 
+// withhold / wait_probes: the test hook of oscar_test_set_wait_fault (-1 / kWaitLimit
+// outside tests)
 __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__restrict__ cov, int32_t max_sweeps,
                                                              float tol, float *__restrict__ rot,
-                                                             float *__restrict__ evals, float *__restrict__ info) {
+                                                             float *__restrict__ evals, float *__restrict__ info,
+                                                             int32_t withhold, uint32_t wait_probes) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   JacobiSmem &S = *reinterpret_cast<JacobiSmem *>(smem_raw);
   __shared__ double wo[kJWarps], wd[kJWarps];
@@ -398,6 +408,8 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
     mbar_init(&S.xbar[0], 1);
     mbar_init(&S.xbar[1], 1);
     S.abort = 0;
+    S.hook_round = batch == 0 && rank == 0 ? withhold : -1;
+    S.wait_probes = wait_probes;
     fence_mbarrier_init();
   }
   for (int e = tid; e < kJRows * kDim; e += kJThreads) {
@@ -454,18 +466,19 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
             aqq[k] += __shfl_xor_sync(0xffffffffu, aqq[k], s);
             apq[k] += __shfl_xor_sync(0xffffffffu, apq[k], s);
           }
+        const uint32_t on = (int32_t)round_no != S.hook_round;  // test hook: pushes skipped
 #pragma unroll
         for (int c = g; c < kJCtas; c += 4) {
           const uint32_t dst = cluster_addr(S.all[buf][m] + 4 * rank, (uint32_t)c);
           const uint32_t bar = cluster_addr(&S.xbar[buf], (uint32_t)c);
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
-            st_async_f64x2(dst + 8u * (uint32_t)(k * kJPairStride), app[k], aqq[k], bar);
-            st_async_f64(dst + 8u * (uint32_t)(k * kJPairStride + 2), apq[k], bar);
+            st_async_f64x2(dst + 8u * (uint32_t)(k * kJPairStride), app[k], aqq[k], bar, on);
+            st_async_f64(dst + 8u * (uint32_t)(k * kJPairStride + 2), apq[k], bar, on);
           }
         }
       }
-      if (!mbar_wait_cluster_bounded(&S.xbar[buf], (round_no >> 1) & 1u)) S.abort = 1;
+      if (!mbar_wait_cluster_bounded(&S.xbar[buf], (round_no >> 1) & 1u, S.wait_probes)) S.abort = 1;
       // (2) cluster sums and the rotation of each pair: lane g adds CTAs g and g + 4, a
       // fixed shuffle tree adds the rest (the same order in every CTA, so every CTA and
       // every lane of the group derives the same rotations)
@@ -670,6 +683,8 @@ __global__ void __launch_bounds__(kJThreads, 1) jacobi_kernel(const float *__res
 using namespace oscar;
 
 namespace oscar {
+int32_t test_hook_withhold();      // oscar_test_set_wait_fault state (attention.cu)
+uint32_t test_hook_wait_probes();
 int gram_tc_launch(const void *x, int64_t n, int32_t h, int64_t xs0, int64_t xs1, int32_t groups,
                    const float *weights, float *cov, int32_t *status, int sm_count, cudaStream_t stream);
 }
@@ -776,8 +791,8 @@ extern "C" int oscar_jacobi_rotations(const float *cov, int32_t batch, int32_t m
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, jacobi_kernel, cov, max_sweeps, tolerance, rotations, eigenvalues, info) !=
-      cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, jacobi_kernel, cov, max_sweeps, tolerance, rotations, eigenvalues, info,
+                         test_hook_withhold(), test_hook_wait_probes()) != cudaSuccess) {
     cudaGetLastError();
     return OSCAR_ERR_LAUNCH;
   }

@@ -1,11 +1,13 @@
-"""The timeout path of the default decode history kernels on the GPU.
+"""The timeout path of the default decode history kernels and the eigensolver on the GPU.
 
 With the test hook `oscar_test_set_wait_fault`, CTA (0, 0, 0) of the history launch never
 issues the copy of its second chunk and every bounded device wait gives up after 4096
 probes.  The launch must return, store OSCAR_ERR_TIMEOUT (4) in the status word, mark the
 aborted CTA's rows empty and leave the context usable: the next step, without the hook,
-matches the oracle with a clear status word.  Nothing here faults or hangs the GPU: the
-withheld copy is never issued, so only the waits run out.
+matches the oracle with a clear status word.  The same hook makes one CTA of the
+eigensolver skip its partial-sum pushes of one round, so its cluster's waits run out.
+Nothing here faults or hangs the GPU: the withheld copy or push is never issued, so only
+the waits run out.
 """
 
 import pytest
@@ -53,3 +55,36 @@ def test_wait_timeout_reports_status_and_context_recovers(cuda_lib, monkeypatch,
     assert kernels.read_status(DEV) == 0
     expect, _ = sc.expected()
     torch.testing.assert_close(out.view(n, 24, 256).float().cpu(), expect, atol=0.035, rtol=0.04)
+
+
+def test_eigensolver_wait_timeout_reports_status_and_context_recovers(cuda_lib):
+    """With the hook, CTA 0 of the first matrix's cluster never pushes its partial sums of
+    round 1 and every wait gives up after 4096 probes: that cluster stops with info status
+    3 in its first sweep and the host publishes nothing; the other matrices of the launch
+    are unaffected, and the next launch without the hook converges to eigvalsh."""
+    from oscar_new_b200 import calibration_kernels as ck
+
+    torch.manual_seed(41)
+    x = torch.randn(3, 512, 256)
+    x[..., :8] *= 5
+    cov = (x.transpose(-1, -2) @ x / 512).to(DEV)
+    rot = torch.empty_like(cov)
+    ev = torch.empty((3, 256), device=DEV)
+    info = torch.zeros((3, 4), device=DEV)
+    lib = _lib.lib()
+    assert lib.oscar_test_set_wait_fault(1, 4096) == 0
+    try:
+        assert lib.oscar_jacobi_rotations(cov.data_ptr(), 3, 12, 1e-7, rot.data_ptr(), ev.data_ptr(),
+                                          info.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        host = info.cpu()
+        assert host[0, 2] == 3 and host[0, 0] == 0, host[0]
+        assert (host[1:, 2] == 0).all() and (host[1:, 1] < 1e-6).all(), host[1:]
+        with pytest.raises(RuntimeError, match="device wait timed out"):
+            ck.calibrated_rotations(cov)
+    finally:
+        assert lib.oscar_test_set_wait_fault(-1, 0) == 0
+    _, ev2, result = ck.calibrated_rotations(cov)
+    assert result["relative_off_diagonal"] < 1e-6
+    ref = torch.linalg.eigvalsh(cov.cpu().double())
+    assert float(((ev2.cpu().double() - ref).abs() / ref.abs()).max()) < 1e-4
