@@ -359,10 +359,10 @@ OSCAR_DEVINL void round_pair(int j, int r, int &p, int &q) {
 // a_pq = v_p . w_q, the entries of the implicit A; its formula, skip rule and
 // convergence test (max|a_pq| / max|a_pp| of a sweep) are the reference's.  Column
 // updates are row-local, so a round needs only the cluster sums of the three dot
-// products (each CTA's sums over its 32 rows, pushed into every CTA over distributed
-// shared memory) and ONE cluster barrier, where the row-rotating form exchanged partner
-// rows with two.  The eigenvalues are the Rayleigh quotients v_p . w_p.  fp64
-// arithmetic (the reference uses fp32).
+// products: each CTA pushes its sums over its 32 rows into every CTA of the cluster with
+// st.async stores that complete on the receiving CTA's mbarrier, and waits (bounded) for
+// the eight pushes it receives; there is no cluster barrier per round.  The eigenvalues
+// are the Rayleigh quotients v_p . w_p.  fp64 arithmetic (the reference uses fp32).
 //
 // The columns live in registers.  Round r pairs seat k with seat 255 - k (pair k,
 // k = 1..127; pair 0 = seat 0 with column 255), and column x sits at seat x - r mod 255:
@@ -373,7 +373,7 @@ OSCAR_DEVINL void round_pair(int j, int r, int &p, int &q) {
 // columns that cross a warp boundary staged in shared memory, so a round reads no
 // matrix data from shared memory.
 OSCAR_DEVINL double rsqrt_f64(double x) {
-  // fp32 seed, two Newton steps: about 46 bits, then the fp64 rounding
+  // fp32 seed (about 23 bits), two Newton steps (about 46 bits, then fp64 precision)
   double y = (double)rsqrtf((float)x);
   y = y * fma(-0.5 * x, y * y, 1.5);
   y = y * fma(-0.5 * x, y * y, 1.5);
