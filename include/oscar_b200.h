@@ -310,8 +310,8 @@ int oscar_normalize(const float *x, int64_t numel, const float *device_denominat
  * Jacobi, all sweeps in one launch (one thread-block cluster per matrix), then
  * ascending eigenpair sort and R = U * H * P_br.  info: fp32[4] = {sweeps,
  * relative_off_diagonal, status (0 ok, 1 not converged, 2 non-finite, 3 a device wait
- * for the cluster's partial sums timed out), 0}.
- * Reference :159-327. */
+ * for the cluster's partial sums timed out), 0}.  batch in [0, 2^20], max_sweeps in
+ * [1, 64]; OSCAR_ERR_INVALID otherwise.  Reference :159-327. */
 int oscar_jacobi_rotations(const float *cov, int32_t batch, int32_t max_sweeps, float tolerance,
                            float *rotations, float *eigenvalues, float *info, void *stream);
 

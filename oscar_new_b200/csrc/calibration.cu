@@ -774,7 +774,9 @@ extern "C" int oscar_normalize(const float *x, int64_t numel, const float *devic
 
 extern "C" int oscar_jacobi_rotations(const float *cov, int32_t batch, int32_t max_sweeps, float tolerance,
                                       float *rotations, float *eigenvalues, float *info, void *stream) {
-  if (batch < 0 || max_sweeps <= 0 || max_sweeps > 64 || !(tolerance > 0.f)) return OSCAR_ERR_INVALID;
+  // batch <= 2^20 keeps the grid (8 CTAs per matrix) inside int range
+  if (batch < 0 || batch > (1 << 20) || max_sweeps <= 0 || max_sweeps > 64 || !(tolerance > 0.f))
+    return OSCAR_ERR_INVALID;
   if (batch == 0) return OSCAR_OK;
   if (!cov || !rotations || !eigenvalues || !info) return OSCAR_ERR_INVALID;
   const int smem = (int)sizeof(JacobiSmem);

@@ -37,6 +37,8 @@ def test_invalid_arguments_are_rejected_without_launch():
     # head_dim != 256 is refused before any device work
     assert handle.oscar_store_int2(None, None, 4, None, None, None, geo, clip, clip, None) == 1
     assert handle.oscar_jacobi_rotations(None, 1, 0, 1e-6, None, None, None, None) == 1
+    assert handle.oscar_jacobi_rotations(None, (1 << 20) + 1, 12, 1e-6, None, None, None, None) == 1
+    assert handle.oscar_jacobi_rotations(None, 0, 12, 1e-6, None, None, None, None) == 0  # nothing to do
     assert handle.oscar_rotate(None, 0, 1, 0, 0, 1, None, 0, 0, None, None) == 1
 
 
